@@ -1,0 +1,677 @@
+// Decode attention over INT8 KV (contiguous or block_table-paged) for sm_100a.
+//
+// Replaces the reference Triton kernels _fused_dequant_attention_kernel,
+// _fused_dequant_attention_split_kernel, _combine_splits_kernel
+// (src/flashspec/triton_fused.py:203-503) and _paged_quant_attention_kernel
+// (src/flashspec/triton_paged.py:120-299).  Same math: scores = q.dequant(k)*sm_scale,
+// masked softmax over min(len, max_seq_len) tokens, out = softmax . dequant(v),
+// fp32 accumulation, fp16 output, empty sequences -> 0 (triton_utils.py:181-186).
+//
+// Design (one CTA = one (request, kv head, split) work item, 4 warps):
+//  * A (page, head) block is 16 tokens x 128 B of K plus the same of V, contiguous in
+//    HBM.  Each warp owns a private ring of kStages stages; one lane issues two 2-D
+//    TMA tile loads (K and V, 128B-swizzled into shared memory) and 4-byte cp.async
+//    copies of the page's scale / zero-point words, all completing on one mbarrier.
+//    Pages of the CTA's range are dealt round-robin to the warps; block_table
+//    entries for the next 64 pages are held in registers and broadcast by shuffle.
+//  * Dequantization is fused into the MMA operands: a byte u (uint8 domain) becomes
+//    the exact fp16 value 1024+u by a byte permute against 0x64 exponent bytes,
+//    and one f16x2 subtract of (1024+zp) gives the exact integer u-zp.  The page
+//    scale is applied to fp32 scores (K) and folded into the fp16 probabilities (V).
+//  * QK^T and PV run on the tensor cores (mma.sync m16n8k16, fp16 in, fp32
+//    accumulate).  QK: M = query heads of the GQA group (<= 8 rows used), N = 8
+//    tokens, K = head_dim; PV: M = head_dim, N = query heads, K = the 16 tokens
+//    of a page.  The S accumulator layout is exactly the PV B-operand layout, so
+//    probabilities never leave registers.  The reduction orders over head_dim and
+//    over tokens are permuted so that every thread reads 16-byte vectors.
+//  * Online softmax in the log2 domain with fp32 (m, l) per query; rescaling only
+//    when some row max grows.  Warps are merged through shared memory at the end.
+//  * Split-K: each split writes (O, LSE) to the workspace; the last CTA of a
+//    (request, kv head) -- found with an atomic ticket -- merges them and writes
+//    the fp16 output (or, in shard mode, the merged (O, LSE) partial).
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <math.h>
+#include <mutex>
+#include <stdint.h>
+
+#include "../../include/flashspec_b200.h"
+#include "common.h"
+#include "ptx.cuh"
+
+namespace fsb {
+
+constexpr int kD = 128;
+constexpr int kPage = 16;
+constexpr int kPageBytes = kPage * kD;     // 2048
+constexpr int kStageBytes = 2 * kPageBytes;  // K + V
+constexpr int kMetaBytes = 32;
+constexpr int kMaxG = 8;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+struct DecodeParams {
+  const __half* q;
+  const float* k_scale;
+  const int16_t* k_zero;
+  const float* v_scale;
+  const int16_t* v_zero;
+  const int64_t* table;
+  const int64_t* lengths;
+  __half* out;
+  float* shard_o;
+  float* shard_lse;
+  float* part_o;
+  float* part_lse;
+  unsigned* counters;
+  uint32_t* status;
+  int B, Hq, Hkv, G, S, cols;
+  int64_t num_blocks;
+  int64_t max_seq_len;
+  int64_t page_begin, page_end;
+  int64_t zp_count;
+  float qk_scale_log2;
+};
+
+template <int kWarps, int kStages>
+struct SmemLayout {
+  static constexpr int kStageRegion = kWarps * kStages * kStageBytes;
+  static constexpr int kMetaRegion = kWarps * kStages * kMetaBytes;
+  static constexpr int kBarRegion = kWarps * kStages * 8;
+  static constexpr int kMergeBytes = kWarps * (2 * kMaxG + kMaxG * kD) * 4;
+  static_assert(kMergeBytes <= kStageRegion, "merge scratch reuses the stage ring");
+  static constexpr int kTotal = 1024 /*alignment slack*/ + kStageRegion + kMetaRegion + kBarRegion;
+};
+
+__device__ __forceinline__ uint32_t kv_to_f16x2(uint32_t x, uint32_t z2) {
+  // x holds bytes [b_lo, *, b_hi, *] (int8 storage of uint8-128).  Keep the low byte of
+  // each half, flip the sign bit (int8 -> uint8 = u) and insert exponent 0x64: the half
+  // is then exactly 1024 + u.  Subtracting 1024 + zp gives the exact integer u - zp.
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(r) : "r"(x), "r"(0x00FF00FFu), "r"(0x64806480u));
+  // 0x6a = (a & b) ^ c
+  return hsub2_u32(r, z2);
+}
+
+template <bool kPaged, int kWarps, int kStages>
+__global__ void __launch_bounds__(kWarps * 32)
+    decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                  const DecodeParams p) {
+  using L = SmemLayout<kWarps, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_u32(smem_raw);
+  const uint32_t base_s = (raw_s + 1023u) & ~1023u;
+  uint8_t* base_p = smem_raw + (base_s - raw_s);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int g = lane >> 2;
+  const int c = lane & 3;
+
+  const uint32_t ring_s = base_s + warp * kStages * kStageBytes;
+  uint32_t* meta_p = reinterpret_cast<uint32_t*>(base_p + L::kStageRegion) + warp * kStages * (kMetaBytes / 4);
+  const uint32_t meta_s = base_s + L::kStageRegion + warp * kStages * kMetaBytes;
+  const uint32_t bar_s = base_s + L::kStageRegion + L::kMetaRegion + warp * kStages * 8;
+
+  // ---- work item ------------------------------------------------------------
+  const int S = p.S;
+  const int blk = blockIdx.x;
+  const int split = blk % S;
+  const int bh = blk / S;
+  const int h = bh % p.Hkv;
+  const int b = bh / p.Hkv;
+
+  int64_t len = p.max_seq_len;
+  if (p.lengths != nullptr) len = min(len, p.lengths[b]);
+  if (len < 0) len = 0;
+  int64_t npages = (len + kPage - 1) / kPage;
+  npages = kPaged ? min(npages, (int64_t)p.cols) : min(npages, p.num_blocks);
+  const int64_t len_eff = min(len, npages * kPage);
+  const int64_t lo = max(p.page_begin, (int64_t)0);
+  const int64_t hi = p.page_end > 0 ? min(p.page_end, npages) : npages;
+  const int64_t span = hi > lo ? hi - lo : 0;
+  const int64_t chunk = (span + S - 1) / S;
+  const int64_t p0 = lo + (int64_t)split * chunk;
+  const int64_t p1 = min(hi, p0 + chunk);
+  const int nj = (p1 - p0 > warp) ? (int)((p1 - p0 - warp + kWarps - 1) / kWarps) : 0;
+
+  if (lane == 0) {
+    for (int st = 0; st < kStages; ++st) mbar_init(bar_s + 8 * st, 2);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (tid == 0) {
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+  }
+  __syncwarp();
+
+  // ---- query fragment: thread (g,c) holds q[g][32c .. 32c+32) -----------------
+  uint32_t qh[16];
+  if (g < p.G) {
+    const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.Hq + (size_t)h * p.G + g) * kD + 32 * c);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = __ldg(qp + i);
+      qh[4 * i + 0] = v.x;
+      qh[4 * i + 1] = v.y;
+      qh[4 * i + 2] = v.z;
+      qh[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) qh[i] = 0u;
+  }
+
+  // ---- page-id window (paged) ---------------------------------------------------
+  const int64_t* trow = kPaged ? p.table + (size_t)b * p.cols : nullptr;
+  auto tbl_load = [&](int jj) -> long long {
+    if (!kPaged || jj >= nj) return -1;
+    return (long long)trow[p0 + warp + (int64_t)jj * kWarps];
+  };
+  long long tcur = tbl_load(lane);
+  long long tnxt = tbl_load(32 + lane);
+  int wbase = 0;
+  const uint64_t policy = l2_policy_evict_first();
+
+  auto issue = [&](int j) {  // warp-uniform
+    long long phys;
+    if (kPaged) {
+      if (j >= wbase + 32) {
+        tcur = tnxt;
+        tnxt = tbl_load(wbase + 64 + lane);
+        wbase += 32;
+      }
+      phys = __shfl_sync(0xffffffffu, tcur, j - wbase);
+    } else {
+      phys = p0 + warp + (int64_t)j * kWarps;
+    }
+    if (lane == 0) {
+      const int st = j % kStages;
+      const uint32_t bar = bar_s + 8 * st;
+      uint32_t* m = meta_p + st * (kMetaBytes / 4);
+      const bool ok = !kPaged || (phys >= 0 && phys < p.num_blocks);
+      if (!ok) {
+        if (phys >= p.num_blocks && p.status != nullptr) atomicOr(p.status, FS_DEV_BAD_PAGE);
+        m[4] = 0u;
+        mbar_arrive(bar);
+        mbar_arrive(bar);
+      } else {
+        const int64_t e = kPaged ? phys * p.Hkv + h : ((int64_t)b * p.Hkv + h) * p.num_blocks + phys;
+        const int32_t row = (int32_t)(e * kPage);
+        uint32_t flags = 1u;
+        const bool word_ok = (e | 1) < p.zp_count;
+        if (word_ok) {
+          flags |= (uint32_t)(e & 1) << 1;
+        } else {
+          m[2] = (uint32_t)(uint16_t)p.k_zero[e];
+          m[3] = (uint32_t)(uint16_t)p.v_zero[e];
+        }
+        m[4] = flags;
+        mbar_arrive_expect_tx(bar, kStageBytes);
+        const uint32_t dst = ring_s + st * kStageBytes;
+        tma_load_2d(dst, &tmk, 0, row, bar, policy);
+        tma_load_2d(dst + kPageBytes, &tmv, 0, row, bar, policy);
+        const uint32_t ms = meta_s + st * kMetaBytes;
+        cp_async_4(ms + 0, p.k_scale + e);
+        cp_async_4(ms + 4, p.v_scale + e);
+        if (word_ok) {
+          cp_async_4(ms + 8, p.k_zero + (e & ~1ll));
+          cp_async_4(ms + 12, p.v_zero + (e & ~1ll));
+        }
+        cp_async_mbar_arrive_noinc(bar);
+      }
+    }
+  };
+
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[i][k] = 0.f;
+  float m_run = -1.0e30f;  // running max (log2 domain), finite so exp2 never sees inf-inf
+  float l_run = 0.f;       // this thread's partial of the softmax denominator
+  int j_done = 0;
+  bool aborted = false;
+
+  const int npre = nj < kStages ? nj : kStages;
+  for (int j = 0; j < npre; ++j) issue(j);
+
+  for (int j = 0; j < nj; ++j) {
+    const int st = j % kStages;
+    if (!mbar_wait_bounded(bar_s + 8 * st, (uint32_t)((j / kStages) & 1), kTimeoutNs)) {
+      aborted = true;
+      j_done = j;
+      if (lane == 0 && p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
+      break;
+    }
+    const volatile uint32_t* m = meta_p + st * (kMetaBytes / 4);
+    const uint32_t flags = m[4];
+    const int64_t lpage = p0 + warp + (int64_t)j * kWarps;
+    if (!(flags & 1u)) {  // unallocated / rejected page: masked like the reference
+      __syncwarp();
+      if (j + kStages < nj) issue(j + kStages);
+      continue;
+    }
+    const float ks = __uint_as_float(m[0]);
+    const float vs = __uint_as_float(m[1]);
+    const uint32_t hi_half = flags & 2u;
+    const uint32_t kz = hi_half ? (m[2] >> 16) : (m[2] & 0xffffu);
+    const uint32_t vz = hi_half ? (m[3] >> 16) : (m[3] & 0xffffu);
+
+    const uint32_t sk = ring_s + st * kStageBytes;
+    const uint32_t sv = sk + kPageBytes;
+    uint4 kr[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int r = g + 8 * nt;
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sk + r * 128 + (((2 * c + e2) ^ (r & 7)) << 4));
+    }
+    uint4 vr[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int r = 2 * c + (t & 1) + 8 * (t >> 1);
+      vr[t] = lds128(sv + r * 128 + ((g ^ (r & 7)) << 4));
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (j + kStages < nj) issue(j + kStages);
+
+    // ---- S = Q K^T (fp16 MMA, exact centred K) --------------------------------
+    const uint32_t zk2 = (0x6400u + (kz & 0x1ffu)) * 0x10001u;
+    const uint32_t zv2 = (0x6400u + (vz & 0x1ffu)) * 0x10001u;
+    float sa[2][2][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int bb = 0; bb < 2; ++bb)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) sa[a][bb][k] = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint4 kv = kr[nt][jj >> 2];
+        const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
+        const uint32_t x = w ^ 0x80808080u;
+        const uint32_t b0 = hsub2_u32(prmt(x, 0x64646464u, 0x5140u), zk2);
+        const uint32_t b1 = hsub2_u32(prmt(x, 0x64646464u, 0x5342u), zk2);
+        mma_16816(sa[nt][jj & 1], qh[2 * jj], 0u, qh[2 * jj + 1], 0u, b0, b1);
+      }
+    }
+    const float f = ks * p.qk_scale_log2;
+    float t[4];
+    t[0] = (sa[0][0][0] + sa[0][1][0]) * f;  // token 2c
+    t[1] = (sa[0][0][1] + sa[0][1][1]) * f;  // token 2c+1
+    t[2] = (sa[1][0][0] + sa[1][1][0]) * f;  // token 8+2c
+    t[3] = (sa[1][0][1] + sa[1][1][1]) * f;  // token 9+2c
+    const int64_t pos0 = lpage * kPage;
+    if (pos0 + kPage > len_eff) {
+      const int tok[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (pos0 + tok[i] >= len_eff) t[i] = -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (__any_sync(0xffffffffu, mx > m_run)) {
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - m_new);
+      m_run = m_new;
+      l_run *= alpha;
+      const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
+      const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc[i][0] *= a0;
+        acc[i][1] *= a1;
+        acc[i][2] *= a0;
+        acc[i][3] *= a1;
+      }
+    }
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = exp2f(t[i] - m_run);
+    l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
+    const uint32_t pb0 = pack_half2(pr[0] * vs, pr[1] * vs);
+    const uint32_t pb1 = pack_half2(pr[2] * vs, pr[3] * vs);
+
+    // ---- O += P V (fp16 MMA, exact centred V) ---------------------------------
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int w = i >> 1;
+      const uint32_t k0 = 2u * (i & 1);
+      const uint32_t sel_a = k0 | (k0 << 4) | ((4u + k0) << 8) | ((4u + k0) << 12);
+      const uint32_t sel_b = (k0 + 1u) | ((k0 + 1u) << 4) | ((5u + k0) << 8) | ((5u + k0) << 12);
+      const uint32_t w0 = w == 0 ? vr[0].x : w == 1 ? vr[0].y : w == 2 ? vr[0].z : vr[0].w;
+      const uint32_t w1 = w == 0 ? vr[1].x : w == 1 ? vr[1].y : w == 2 ? vr[1].z : vr[1].w;
+      const uint32_t w2 = w == 0 ? vr[2].x : w == 1 ? vr[2].y : w == 2 ? vr[2].z : vr[2].w;
+      const uint32_t w3 = w == 0 ? vr[3].x : w == 1 ? vr[3].y : w == 2 ? vr[3].z : vr[3].w;
+      const uint32_t a0 = kv_to_f16x2(prmt(w0, w1, sel_a), zv2);
+      const uint32_t a1 = kv_to_f16x2(prmt(w0, w1, sel_b), zv2);
+      const uint32_t a2 = kv_to_f16x2(prmt(w2, w3, sel_a), zv2);
+      const uint32_t a3 = kv_to_f16x2(prmt(w2, w3, sel_b), zv2);
+      mma_16816(acc[i], a0, a1, a2, a3, pb0, pb1);
+    }
+  }
+
+  if (aborted) {  // drain our own copies in flight (bounded) before the ring is reused
+    const int jmax = min(nj, j_done + kStages);
+    for (int j = j_done; j < jmax; ++j)
+      (void)mbar_wait_bounded(bar_s + 8 * (j % kStages), (uint32_t)((j / kStages) & 1), kTimeoutNs / 16);
+  }
+
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+
+  // ---- merge the warps of this CTA through shared memory ------------------------
+  __syncthreads();  // every warp is done with its ring
+  float* ms = reinterpret_cast<float*>(base_p);
+  float* ls = ms + kWarps * kMaxG;
+  float* accs = ls + kWarps * kMaxG;  // [kWarps][kMaxG][kD]
+  if (c == 0) {
+    ms[warp * kMaxG + g] = m_run;
+    ls[warp * kMaxG + g] = l_run;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = 16 * g + 2 * i;
+    float* a0p = accs + (warp * kMaxG + 2 * c) * kD;
+    float* a1p = accs + (warp * kMaxG + 2 * c + 1) * kD;
+    a0p[d] = acc[i][0];
+    a1p[d] = acc[i][1];
+    a0p[d + 1] = acc[i][2];
+    a1p[d + 1] = acc[i][3];
+  }
+  __syncthreads();
+
+  const bool any_abort = __syncthreads_or(aborted ? 1 : 0);
+  if (any_abort) return;  // status word carries FS_DEV_TIMEOUT; outputs are not written
+
+  const int nout = p.G * kD;
+  const float kLn2 = 0.6931471805599453f;
+  for (int idx = tid; idx < nout; idx += kWarps * 32) {
+    const int qg = idx >> 7;
+    const int d = idx & (kD - 1);
+    float M = -1.0e30f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ms[w * kMaxG + qg]);
+    float Lsum = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float sc = exp2f(ms[w * kMaxG + qg] - M);
+      Lsum += ls[w * kMaxG + qg] * sc;
+      O += accs[(w * kMaxG + qg) * kD + d] * sc;
+    }
+    const float o = Lsum > 0.f ? O / Lsum : 0.f;
+    const float lse = Lsum > 0.f ? (M + log2f(Lsum)) * kLn2 : -INFINITY;
+    const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
+    if (S == 1) {
+      if (p.shard_o != nullptr) {
+        p.shard_o[row * kD + d] = o;
+        if (d == 0) p.shard_lse[row] = lse;
+      } else {
+        p.out[row * kD + d] = __float2half_rn(o);
+      }
+    } else {
+      const size_t prow = ((size_t)bh * S + split) * p.G + qg;
+      p.part_o[prow * kD + d] = o;
+      if (d == 0) p.part_lse[prow] = lse;
+    }
+  }
+  if (S == 1) return;
+
+  // ---- split-K: the last CTA of this (request, kv head) merges -------------------
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned ticket = atomicAdd(p.counters + bh, 1u);
+    s_last = (ticket == (unsigned)(S - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = tid; idx < nout; idx += kWarps * 32) {
+    const int qg = idx >> 7;
+    const int d = idx & (kD - 1);
+    const size_t prow0 = (size_t)bh * S * p.G + qg;
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(p.part_lse + prow0 + (size_t)s2 * p.G));
+    float W = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int s2 = 0; s2 < S; ++s2) {
+        const size_t pr = prow0 + (size_t)s2 * p.G;
+        const float lse = __ldcg(p.part_lse + pr);
+        const float w = lse == -INFINITY ? 0.f : expf(lse - M);
+        W += w;
+        O += w * __ldcg(p.part_o + pr * kD + d);
+      }
+    }
+    const float o = W > 0.f ? O / W : 0.f;
+    const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
+    if (p.shard_o != nullptr) {
+      p.shard_o[row * kD + d] = o;
+      if (d == 0) p.shard_lse[row] = W > 0.f ? M + logf(W) : -INFINITY;
+    } else {
+      p.out[row * kD + d] = __float2half_rn(o);
+    }
+  }
+  if (tid == 0) p.counters[bh] = 0u;  // leave the ticket clean for the next call
+}
+
+// ---------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------
+
+constexpr int kWarpsCfg = 4;
+constexpr int kStagesCfg = 4;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// View of an int8 KV array as rows of 128 bytes; one box = one 16-row page block.
+static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return FS_ERR_CUDA;
+  cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)kD};
+  cuuint32_t box[2] = {(cuuint32_t)kD, (cuuint32_t)kPage};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? FS_OK : FS_ERR_CUDA;
+}
+
+template <bool kPaged>
+static int configure_kernel(int device) {
+  static bool done[2][kMaxDevices] = {};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= kMaxDevices) return FS_ERR_CUDA;
+  if (done[kPaged][device]) return FS_OK;
+  using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel<kPaged, kWarpsCfg, kStagesCfg>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kTotal);
+  if (e != cudaSuccess) return FS_ERR_CUDA;
+  done[kPaged][device] = true;
+  return FS_OK;
+}
+
+static int resident_ctas(int device) {
+  static int cached[kMaxDevices] = {};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[device] > 0) return cached[device];
+  int per_sm = 0;
+  using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<true, kWarpsCfg, kStagesCfg>,
+                                                    kWarpsCfg * 32, Lay::kTotal) != cudaSuccess ||
+      per_sm <= 0)
+    per_sm = 1;
+  cached[device] = per_sm * device_sm_count(device);
+  return cached[device];
+}
+
+static int64_t max_pages_of(const FsDecodeArgs* a) {
+  int64_t np = ((int64_t)a->max_seq_len + kPage - 1) / kPage;
+  if (a->layout == FS_LAYOUT_PAGED)
+    np = np < a->table_cols ? np : a->table_cols;
+  else
+    np = np < a->num_blocks ? np : a->num_blocks;
+  int64_t lo = a->page_begin > 0 ? a->page_begin : 0;
+  int64_t hi = a->page_end > 0 && a->page_end < np ? a->page_end : np;
+  return hi > lo ? hi - lo : 0;
+}
+
+static int resolve_splits(const FsDecodeArgs* a, int device) {
+  if (a->num_splits > 0) return a->num_splits;
+  const int64_t pairs = (int64_t)a->batch * a->kv_heads;
+  const int64_t maxp = max_pages_of(a);
+  const int64_t target = 4LL * resident_ctas(device);
+  int64_t s = (target + pairs - 1) / (pairs > 0 ? pairs : 1);
+  const int64_t cap = maxp / (kWarpsCfg * 4);  // at least ~4 pages per warp
+  if (s > cap) s = cap;
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return (int)s;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static size_t workspace_for(const FsDecodeArgs* a, int splits) {
+  if (splits <= 1) return 0;
+  const size_t G = (size_t)(a->q_heads / a->kv_heads);
+  const size_t units = (size_t)a->batch * a->kv_heads * splits * G;
+  return align256(units * kD * 4) + align256(units * 4);
+}
+
+static int validate(const FsDecodeArgs* a, int layout) {
+  if (a == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  if (a->layout != layout) return FS_ERR_INVALID_ARGUMENT;
+  if (a->batch <= 0 || a->q_heads <= 0 || a->kv_heads <= 0) return FS_ERR_INVALID_ARGUMENT;
+  if (a->q_heads % a->kv_heads) return FS_ERR_INVALID_ARGUMENT;
+  const int G = a->q_heads / a->kv_heads;
+  if (G > kMaxG) return FS_ERR_UNSUPPORTED;
+  if (a->head_dim != kD || a->block_size != kPage) return FS_ERR_UNSUPPORTED;
+  if (a->q == nullptr || a->k_values == nullptr || a->v_values == nullptr || a->k_scale == nullptr ||
+      a->v_scale == nullptr || a->k_zero == nullptr || a->v_zero == nullptr)
+    return FS_ERR_INVALID_ARGUMENT;
+  if (a->shard_o == nullptr && a->out == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  if ((a->shard_o == nullptr) != (a->shard_lse == nullptr)) return FS_ERR_INVALID_ARGUMENT;
+  if (a->num_blocks <= 0 || a->max_seq_len < 0) return FS_ERR_INVALID_ARGUMENT;
+  if (layout == FS_LAYOUT_PAGED) {
+    if (a->block_table == nullptr || a->lengths == nullptr || a->table_cols <= 0) return FS_ERR_INVALID_ARGUMENT;
+    if ((uint64_t)a->num_blocks * a->kv_heads * kPage >= (1ull << 31)) return FS_ERR_UNSUPPORTED;
+  } else {
+    if ((uint64_t)a->batch * a->kv_heads * a->num_blocks * kPage >= (1ull << 31)) return FS_ERR_UNSUPPORTED;
+    if ((int64_t)a->max_seq_len > a->num_blocks * kPage) return FS_ERR_INVALID_ARGUMENT;
+  }
+  if ((reinterpret_cast<uintptr_t>(a->k_values) | reinterpret_cast<uintptr_t>(a->v_values) |
+       reinterpret_cast<uintptr_t>(a->q)) & 15)
+    return FS_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(a->k_zero) | reinterpret_cast<uintptr_t>(a->v_zero) |
+       reinterpret_cast<uintptr_t>(a->k_scale) | reinterpret_cast<uintptr_t>(a->v_scale)) & 3)
+    return FS_ERR_ALIGNMENT;
+  return FS_OK;
+}
+
+template <bool kPaged>
+static int launch_decode(const FsDecodeArgs* a, void* stream) {
+  int st = validate(a, kPaged ? FS_LAYOUT_PAGED : FS_LAYOUT_CONTIGUOUS);
+  if (st != FS_OK) return st;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
+  if ((st = configure_kernel<kPaged>(device)) != FS_OK) return st;
+  const int splits = resolve_splits(a, device);
+  const size_t need = workspace_for(a, splits);
+  if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need)) return FS_ERR_WORKSPACE;
+  if (splits > 1 && (a->tickets == nullptr || a->ticket_count < (int64_t)a->batch * a->kv_heads))
+    return FS_ERR_WORKSPACE;
+
+  const uint64_t rows = kPaged ? (uint64_t)a->num_blocks * a->kv_heads * kPage
+                               : (uint64_t)a->batch * a->kv_heads * a->num_blocks * kPage;
+  CUtensorMap tmk, tmv;
+  if ((st = make_kv_map(&tmk, a->k_values, rows)) != FS_OK) return st;
+  if ((st = make_kv_map(&tmv, a->v_values, rows)) != FS_OK) return st;
+
+  DecodeParams p{};
+  p.q = reinterpret_cast<const __half*>(a->q);
+  p.k_scale = a->k_scale;
+  p.k_zero = a->k_zero;
+  p.v_scale = a->v_scale;
+  p.v_zero = a->v_zero;
+  p.table = a->block_table;
+  p.lengths = a->lengths;
+  p.out = reinterpret_cast<__half*>(a->out);
+  p.shard_o = a->shard_o;
+  p.shard_lse = a->shard_lse;
+  p.status = a->device_status;
+  p.B = a->batch;
+  p.Hq = a->q_heads;
+  p.Hkv = a->kv_heads;
+  p.G = a->q_heads / a->kv_heads;
+  p.S = splits;
+  p.cols = a->table_cols;
+  p.num_blocks = a->num_blocks;
+  p.max_seq_len = a->max_seq_len;
+  p.page_begin = a->page_begin;
+  p.page_end = a->page_end;
+  p.zp_count = kPaged ? a->num_blocks * a->kv_heads : (int64_t)a->batch * a->kv_heads * a->num_blocks;
+  p.qk_scale_log2 = a->sm_scale * 1.4426950408889634f;
+  if (splits > 1) {
+    const size_t G = (size_t)p.G;
+    const size_t units = (size_t)a->batch * a->kv_heads * splits * G;
+    uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+    p.part_o = reinterpret_cast<float*>(ws);
+    p.part_lse = reinterpret_cast<float*>(ws + align256(units * kD * 4));
+    p.counters = reinterpret_cast<unsigned*>(a->tickets);
+  }
+  using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
+  const int64_t grid = (int64_t)a->batch * a->kv_heads * splits;
+  if (grid >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
+  decode_kernel<kPaged, kWarpsCfg, kStagesCfg><<<(unsigned)grid, kWarpsCfg * 32, Lay::kTotal,
+                                                 reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
+  return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
+}
+
+}  // namespace fsb
+
+extern "C" {
+
+int fs_decode_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* splits_out) {
+  if (a == nullptr || bytes == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  int st = fsb::validate(a, a->layout);
+  if (st != FS_OK) return st;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
+  const int s = fsb::resolve_splits(a, device);
+  *bytes = fsb::workspace_for(a, s);
+  if (splits_out) *splits_out = s;
+  return FS_OK;
+}
+
+int fs_fused_decode(const FsDecodeArgs* args, void* stream) { return fsb::launch_decode<false>(args, stream); }
+
+int fs_paged_decode(const FsDecodeArgs* args, void* stream) { return fsb::launch_decode<true>(args, stream); }
+
+}  // extern "C"

@@ -1,0 +1,171 @@
+/*
+ * flashspec_b200 -- C ABI of the B200 (sm_100a) INT8 decode-attention library.
+ *
+ * Plain C: raw device pointers, sizes and a CUDA stream passed as void*.  No torch
+ * types cross this boundary.  Every entry point is asynchronous on the given
+ * stream, never synchronises, and returns an FsStatus (0 = ok).
+ *
+ * Data formats are those of the FlashSpec reference (src/flashspec/quant.py:9-43,
+ * paged.py:258-300): affine INT8 per (page|block, head): values int8 = uint8-128,
+ * fp32 scale, int16 zero_point in the uint8 domain, one (scale, zp) per
+ * [block_size x head_dim] block.
+ *   contiguous KV : values [B, Hkv, nblk, 16, D], scale/zp [B, Hkv, nblk]
+ *   paged KV pool : values [P, Hkv, 16, D],        scale/zp [P, Hkv]
+ *   block_table   : int64 [B, cols], -1 = unallocated; lengths int64 [B]
+ *   q / out       : fp16 [B, Hq, D]; q head h reads kv head h / (Hq/Hkv)
+ * Current kernel limits: D = 128, block (page) size 16, Hq/Hkv in 1..8.
+ */
+#ifndef FLASHSPEC_B200_H_
+#define FLASHSPEC_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FS_ABI_VERSION 1
+
+typedef enum FsStatus {
+  FS_OK = 0,
+  FS_ERR_INVALID_ARGUMENT = 1, /* shape / size / pointer inconsistency      */
+  FS_ERR_UNSUPPORTED = 2,      /* valid input outside the kernel's limits    */
+  FS_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed          */
+  FS_ERR_WORKSPACE = 4,        /* workspace missing or too small             */
+  FS_ERR_ALIGNMENT = 5         /* pointer not aligned as the kernel needs    */
+} FsStatus;
+
+/* bits OR-ed into the optional device status word by kernels */
+#define FS_DEV_BAD_PAGE 1u /* block_table entry outside [0, num_pages): page skipped */
+#define FS_DEV_TIMEOUT 2u  /* a bounded wait gave up; outputs of that CTA invalid   */
+
+typedef enum FsDtype { FS_F16 = 0, FS_BF16 = 1, FS_F32 = 2 } FsDtype;
+
+typedef enum FsKvLayout { FS_LAYOUT_CONTIGUOUS = 0, FS_LAYOUT_PAGED = 1 } FsKvLayout;
+
+/* Arguments of one decode-attention call (one query token per request). */
+typedef struct FsDecodeArgs {
+  int32_t layout;             /* FsKvLayout                                          */
+  const void* q;              /* fp16 [B, Hq, D]                                     */
+  const int8_t* k_values;     /* see layouts above; 16-byte aligned                  */
+  const float* k_scale;
+  const int16_t* k_zero;      /* 4-byte aligned                                      */
+  const int8_t* v_values;
+  const float* v_scale;
+  const int16_t* v_zero;
+  const int64_t* block_table; /* paged: [B, table_cols]; contiguous: NULL            */
+  const int64_t* lengths;     /* [B]; NULL (contiguous only) = every request is seq_len */
+  void* out;                  /* fp16 [B, Hq, D]; unused when shard_o is set          */
+  int32_t batch, q_heads, kv_heads, head_dim, block_size;
+  int64_t num_blocks;         /* paged: physical pages P; contiguous: nblk per (b,h)  */
+  int32_t table_cols;         /* paged only                                          */
+  int32_t max_seq_len;        /* paged: cache.max_seq_len; contiguous: seq_len        */
+  int32_t num_splits;         /* split-K factor; 0 = library policy                   */
+  float sm_scale;             /* softmax scale, normally 1/sqrt(D)                    */
+  /* optional logical page window [page_begin, page_end) per request (sequence
+   * sharding across GPUs); page_end <= 0 means "to the end" */
+  int64_t page_begin, page_end;
+  /* optional partial outputs: when shard_o != NULL the call writes the normalised
+   * partial O fp32 [B, Hq, D] and LSE fp32 [B, Hq] (natural log, -inf if empty)
+   * instead of `out`, for a later fs_merge_partials */
+  float* shard_o;
+  float* shard_lse;
+  void* workspace;            /* device scratch for split partials,
+                                 fs_decode_workspace_size() bytes (any contents)   */
+  size_t workspace_bytes;
+  uint32_t* tickets;          /* device merge counters, >= batch*kv_heads entries when
+                                 num_splits > 1; must be zero at call time; every call
+                                 that completes leaves them zero                    */
+  int64_t ticket_count;
+  uint32_t* device_status;    /* optional device word receiving FS_DEV_* bits         */
+} FsDecodeArgs;
+
+/* Library version / ABI check. */
+int fs_abi_version(void);
+const char* fs_status_string(int status);
+
+/* Bytes of workspace a call with these arguments needs (0 when num_splits
+ * resolves to 1; the call then needs batch*kv_heads zeroed tickets as well).  Resolves num_splits==0 with the library policy and reports
+ * the value used in *splits_out (may be NULL). */
+int fs_decode_workspace_size(const FsDecodeArgs* args, size_t* bytes, int32_t* splits_out);
+
+/* Contiguous INT8 KV decode attention.
+ * Replaces _run_fused_dequant_attention_triton (src/flashspec/triton_fused.py:604-761)
+ * i.e. the kernels _fused_dequant_attention_kernel / _split_kernel /
+ * _combine_splits_kernel (triton_fused.py:203-503).  args->layout must be
+ * FS_LAYOUT_CONTIGUOUS. */
+int fs_fused_decode(const FsDecodeArgs* args, void* stream);
+
+/* Paged INT8 KV decode attention through block_table.
+ * Replaces _run_paged_quant_attention_triton (src/flashspec/triton_paged.py:338-450)
+ * and _paged_quant_attention_kernel (triton_paged.py:120-299), adding split-K,
+ * GQA and page windows.  args->layout must be FS_LAYOUT_PAGED. */
+int fs_paged_decode(const FsDecodeArgs* args, void* stream);
+
+/* Log-sum-exp merge of n_parts partial results (split-K partials, or per-GPU
+ * shards gathered over NVLink).  o_parts fp32 [n_parts, rows, head_dim],
+ * lse_parts fp32 [n_parts, rows]; writes out [rows, head_dim] as out_dtype
+ * (FS_F16 or FS_F32).  Rows whose partials are all empty produce 0.
+ * Same math as _combine_splits_kernel (src/flashspec/triton_fused.py:446-503). */
+int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows,
+                      int32_t head_dim, void* out, int32_t out_dtype, void* stream);
+
+/* Affine INT8 quantization of x [n_lead, seq_len, head_dim] (dtype x_dtype,
+ * contiguous) in blocks of block_size tokens, zero-padding the last block:
+ * values [n_lead, nblk, block_size, head_dim], scale/zero_point [n_lead, nblk].
+ * Bit-exact with quantize_int8_per_block (src/flashspec/quant.py:94-165). */
+typedef struct FsQuantizeArgs {
+  const void* x;
+  int32_t x_dtype;
+  int64_t n_lead;
+  int32_t seq_len, head_dim, block_size;
+  int8_t* values;
+  float* scale;
+  int16_t* zero_point;
+} FsQuantizeArgs;
+int fs_quantize_blocks(const FsQuantizeArgs* args, void* stream);
+
+/* One page rewrite: rows [dst_row, dst_row+n_rows) of physical page `page`
+ * take tokens [src_t, src_t+n_rows) of source request src_b; the other rows
+ * are the page's dequantized current contents (from_zero=0, i.e. stale rows of
+ * a reused page are kept) or zeros (from_zero=1); then the page is requantized. */
+typedef struct FsPageUpdate {
+  int64_t page;
+  int32_t src_b, src_t, dst_row, n_rows, from_zero, reserved;
+} FsPageUpdate;
+
+typedef struct FsPageUpdateArgs {
+  const FsPageUpdate* items;  /* DEVICE array [n_items]; pages distinct            */
+  int32_t n_items;
+  const void* k_src;          /* [Bsrc, H, T, D] with the strides below (elements) */
+  const void* v_src;
+  int32_t src_dtype;
+  int64_t src_stride_b, src_stride_h, src_stride_t; /* D stride must be 1 */
+  int32_t heads, head_dim, block_size;
+  int64_t num_pages;          /* pool pages (bounds of items[].page)               */
+  /* pool read before the update (may equal the *_out pointers: in place)          */
+  const int8_t* k_values_in; const float* k_scale_in; const int16_t* k_zero_in;
+  const int8_t* v_values_in; const float* v_scale_in; const int16_t* v_zero_in;
+  int8_t* k_values_out; float* k_scale_out; int16_t* k_zero_out;
+  int8_t* v_values_out; float* v_scale_out; int16_t* v_zero_out;
+} FsPageUpdateArgs;
+
+/* Page append / prefill with re-quantization, bit-exact with the reference
+ * allocator (PagedKVAllocator.add_request / append_request / _write_quantized_block,
+ * src/flashspec/paged.py:66-136,226-255) and with the whole-store requantization of
+ * PagedKVCache.append (paged.py:463-557) when every page is listed. */
+int fs_page_update(const FsPageUpdateArgs* args, void* stream);
+
+/* Dequantize pages into fp32 [n_pages_listed, H, block_size, D]; pages is a device
+ * int64 list (entries < 0 give zeros).  Same arithmetic as
+ * dequantize_int8_per_block (src/flashspec/quant.py:168-204). */
+int fs_dequantize_pages(const int8_t* values, const float* scale, const int16_t* zero_point,
+                        const int64_t* pages, int64_t n_pages_listed, int64_t num_pages, int32_t heads,
+                        int32_t block_size, int32_t head_dim, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHSPEC_B200_H_ */

@@ -1,0 +1,348 @@
+"""GPU parity of the CUDA path against the golden vectors (recorded from the
+reference) and the CPU oracle.
+
+Tolerances: attention outputs (fp16) within max-abs 2e-3 and rel 1e-2 of the
+reference, i.e. |got - ref| <= 2e-3 + 1e-2 * |ref| elementwise; quantized bytes,
+scales, zero points, block tables and allocator state bit-exact."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import flashspec_oracle as O
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def fs():
+    import flashspec_b200
+
+    return flashspec_b200
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    torch.manual_seed(0)
+
+
+def dev(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def qt_dev(g, prefix):
+    f = fs()
+    return f.QuantizedTensor(dev(g[f"{prefix}.values"]), dev(g[f"{prefix}.scale"]), dev(g[f"{prefix}.zero_point"]),
+                             int(g[f"{prefix}.block_size"]), tuple(int(x) for x in g[f"{prefix}.original_shape"]))
+
+
+def close(got: torch.Tensor, ref, atol=ATOL, rtol=RTOL):
+    ref_t = torch.as_tensor(np.asarray(ref, dtype=np.float32))
+    got_f = got.detach().float().cpu()
+    err = (got_f - ref_t).abs()
+    bound = atol + rtol * ref_t.abs()
+    assert torch.all(err <= bound), f"max abs err {err.max().item():.3e}"
+    return err.max().item()
+
+
+def same_quant(qt, oq):
+    np.testing.assert_array_equal(qt.values.cpu().numpy(), oq.values)
+    np.testing.assert_array_equal(qt.scale.cpu().numpy().view(np.uint32), oq.scale.view(np.uint32))
+    np.testing.assert_array_equal(qt.zero_point.cpu().numpy(), oq.zero_point)
+
+
+# ---------------------------------------------------------------------------------
+# quantizer
+# ---------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name,bs", [("quant_fp32_b8", 8), ("quant_fp16_b16", 16), ("quant_edge_b16", 16)])
+def test_quantize_matches_reference_bit_exact(name, bs):
+    g = load_golden(name)
+    q = fs().quantize_int8_per_block(dev(g["x"]), bs)
+    same_quant(q, g.quant("q"))
+    assert tuple(q.original_shape) == tuple(int(x) for x in g["q.original_shape"])
+
+
+def test_quantize_random_bf16_and_odd_shapes_vs_oracle():
+    rng = np.random.default_rng(1)
+    for shape, bs in [((3, 5, 33, 128), 16), ((2, 7, 64), 16), ((4, 1, 17, 96), 4)]:
+        x = (rng.standard_normal(shape) * rng.uniform(0.01, 50)).astype(np.float32)
+        xt = dev(x).to(torch.bfloat16)
+        q = fs().quantize_int8_per_block(xt, bs)
+        same_quant(q, O.quantize_int8_per_block(xt.float().cpu().numpy(), bs))
+
+
+# ---------------------------------------------------------------------------------
+# contiguous backend
+# ---------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("name", ["fused_s129", "fused_s1500", "fused_nolen_s200"])
+def test_fused_matches_reference_golden(name):
+    g = load_golden(name)
+    lengths = dev(g["lengths"]) if "lengths" in g else None
+    out, stats = fs().fused_dequant_attention_cuda(dev(g["q"]), qt_dev(g, "kq"), qt_dev(g, "vq"), lengths,
+                                                   return_stats=True)
+    assert out.dtype == torch.float16 and tuple(out.shape) == g["q"].shape
+    close(out, g["out"])
+    assert stats["materializes_dense_kv"] == 0.0
+    assert stats["quant_kv_bytes"] == float(g["quant_kv_bytes"])
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 64])
+def test_fused_split_k_invariance(splits):
+    g = load_golden("fused_s1500")
+    out = fs().fused_dequant_attention_cuda(dev(g["q"]), qt_dev(g, "kq"), qt_dev(g, "vq"), dev(g["lengths"]),
+                                            num_splits=splits)
+    close(out, g["out"])
+
+
+# ---------------------------------------------------------------------------------
+# paged backend
+# ---------------------------------------------------------------------------------
+
+
+def paged_from_golden(g, key_table="block_table"):
+    return fs().PagedKVCache(qt_dev(g, "kq"), qt_dev(g, "vq"), dev(g[key_table]), dev(g["lengths"]), 16,
+                             int(g["max_seq_len"]))
+
+
+@pytest.mark.parametrize("layout", ["contiguous", "shuffled", "interleaved"])
+def test_paged_matches_reference_golden(layout):
+    g = load_golden(f"paged_{layout}")
+    out, stats = fs().paged_quant_attention_cuda(dev(g["q"]), paged_from_golden(g), return_stats=True)
+    close(out, g["out"])
+    assert stats["physical_blocks"] == float(g["physical_blocks"])
+    assert stats["quant_kv_bytes"] == float(g["quant_kv_bytes"])
+    assert stats["materializes_dense_kv"] == 0.0
+
+
+def test_paged_gqa_matches_reference_golden():
+    g = load_golden("paged_gqa4")
+    out = fs().paged_quant_attention_cuda(dev(g["q"]), paged_from_golden(g))
+    close(out, g["out"])
+
+
+def test_paged_from_dense_on_gpu_matches_reference_layout():
+    g = load_golden("paged_shuffled")
+    table = g["block_table"].reshape(-1)
+    perm = np.empty_like(table)
+    perm[table] = np.arange(table.size)
+    cache = fs().PagedKVCache.from_dense(dev(g["k"]), dev(g["v"]), 16, lengths=dev(g["lengths"]),
+                                         block_table_pattern="shuffled", perm=dev(perm))
+    same_quant(cache.k_quant, g.quant("kq"))
+    same_quant(cache.v_quant, g.quant("vq"))
+    np.testing.assert_array_equal(cache.block_table.cpu().numpy(), g["block_table"])
+
+
+def _random_paged(rng, b, hq, hkv, lens, slack=3, layout="shuffled"):
+    smax = max(max(lens), 1)
+    q = rng.standard_normal((b, hq, 128)).astype(np.float16)
+    k = rng.standard_normal((b, hkv, smax, 128)).astype(np.float16)
+    v = rng.standard_normal((b, hkv, smax, 128)).astype(np.float16)
+    bps = (smax + 15) // 16
+    total = b * bps + slack
+    perm = rng.permutation(total)[: b * bps] if layout == "shuffled" else np.arange(b * bps)
+    oc = O.paged_from_dense(k, v, 16, lengths=np.array(lens), pattern="contiguous")
+    # scatter logical pages to physical slots `perm` of a pool with slack pages
+    pool_k = O.quantize_int8_per_block(np.zeros((total, hkv, 16, 128), np.float32), 16)
+    pool_v = O.quantize_int8_per_block(np.zeros((total, hkv, 16, 128), np.float32), 16)
+    for src, dst in enumerate(perm):
+        for pool, part in ((pool_k, oc.k_quant), (pool_v, oc.v_quant)):
+            pool.values[dst] = part.values[src]
+            pool.scale[dst] = part.scale[src]
+            pool.zero_point[dst] = part.zero_point[src]
+    table = perm.reshape(b, bps).astype(np.int64)
+    ocache = O.OPagedCache(pool_k, pool_v, table, np.array(lens, np.int64), 16, smax)
+    return q, ocache
+
+
+def _cache_dev(oc):
+    f = fs()
+    qk = f.QuantizedTensor(dev(oc.k_quant.values), dev(oc.k_quant.scale), dev(oc.k_quant.zero_point), 16,
+                           oc.k_quant.original_shape)
+    qv = f.QuantizedTensor(dev(oc.v_quant.values), dev(oc.v_quant.scale), dev(oc.v_quant.zero_point), 16,
+                           oc.v_quant.original_shape)
+    return f.PagedKVCache(qk, qv, dev(oc.block_table), dev(oc.lengths), 16, oc.max_seq_len)
+
+
+@pytest.mark.parametrize("hq,hkv", [(4, 4), (8, 4), (8, 2), (16, 2), (8, 1)])
+@pytest.mark.parametrize("splits", [0, 1, 5])
+def test_paged_random_ragged_gqa_vs_oracle(hq, hkv, splits):
+    rng = np.random.default_rng(hq * 100 + hkv * 10 + splits)
+    lens = [1, 16, 17, 250, 31, 512, 100]
+    q, oc = _random_paged(rng, len(lens), hq, hkv, lens)
+    out = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc), num_splits=splits or None)
+    close(out, O.paged_quant_attention(q, oc))
+
+
+def test_paged_zero_length_outputs_zero():
+    rng = np.random.default_rng(3)
+    q, oc = _random_paged(rng, 3, 4, 4, [40, 0, 7])
+    oc.lengths[1] = 0
+    out = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc), num_splits=4)
+    assert torch.all(out[1] == 0)
+    ref = O.paged_quant_attention(q, oc)
+    close(out[[0, 2]], ref[[0, 2]])
+
+
+def test_paged_unallocated_table_entries_are_masked():
+    rng = np.random.default_rng(4)
+    q, oc = _random_paged(rng, 2, 4, 4, [64, 20])
+    # request 1 only needs 2 pages: the rest of its row is -1 in a real allocator
+    oc.block_table[1, 2:] = -1
+    out = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc))
+    close(out, O.paged_quant_attention(q, oc))
+
+
+def test_paged_bad_page_index_is_reported_not_read():
+    rng = np.random.default_rng(5)
+    q, oc = _random_paged(rng, 2, 4, 4, [64, 64])
+    ok = O.paged_quant_attention(q, oc)
+    n_pages = oc.k_quant.values.shape[0]
+    oc.block_table[0, 1] = n_pages + 1000  # beyond the pool: the kernel must skip it
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc), device_status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 1
+    close(out[1], ok[1])
+
+
+def test_paged_layout_invariance_is_bit_exact():
+    """The same logical pages in a different physical order give identical bits."""
+    rng = np.random.default_rng(6)
+    q, oc_a = _random_paged(rng, 3, 8, 2, [300, 129, 77], layout="contiguous")
+    perm = rng.permutation(oc_a.k_quant.values.shape[0])
+    inv = np.empty_like(perm)
+    inv[perm] = np.arange(perm.size)
+    sh = lambda qt: O.OQuant(qt.values[perm], qt.scale[perm], qt.zero_point[perm], 16, qt.original_shape)
+    oc_b = O.OPagedCache(sh(oc_a.k_quant), sh(oc_a.v_quant), inv[oc_a.block_table], oc_a.lengths, 16,
+                         oc_a.max_seq_len)
+    a = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc_a), num_splits=3)
+    b = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc_b), num_splits=3)
+    assert torch.equal(a, b)
+    c = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc_a), num_splits=3)
+    assert torch.equal(a, c)  # deterministic rerun
+
+
+def test_paged_page_windows_and_merge_equal_full():
+    rng = np.random.default_rng(7)
+    q, oc = _random_paged(rng, 2, 16, 2, [700, 333])
+    cache = _cache_dev(oc)
+    full = fs().paged_quant_attention_cuda(dev(q), cache)
+    bounds = [0, 5, 19, 30, 44]
+    os_, ls_ = [], []
+    for lo, hi in zip(bounds[:-1], bounds[1:]):
+        o = torch.empty(q.shape, dtype=torch.float32, device="cuda")
+        lse = torch.empty(q.shape[:2], dtype=torch.float32, device="cuda")
+        fs().paged_quant_attention_cuda(dev(q), cache, page_range=(lo, hi), partial_out=(o, lse))
+        os_.append(o)
+        ls_.append(lse)
+    merged = fs().merge_partials(torch.stack(os_), torch.stack(ls_))
+    close(merged, full.float().cpu().numpy(), atol=1e-3, rtol=1e-3)
+    close(merged, O.paged_quant_attention(q, oc))
+    # a window past every request's end is empty: LSE -inf, O = 0
+    o = torch.empty(q.shape, dtype=torch.float32, device="cuda")
+    lse = torch.empty(q.shape[:2], dtype=torch.float32, device="cuda")
+    fs().paged_quant_attention_cuda(dev(q), cache, page_range=(100, 200), partial_out=(o, lse))
+    assert torch.all(torch.isneginf(lse)) and torch.all(o == 0)
+
+
+def test_validation_errors():
+    f = fs()
+    g = load_golden("paged_contiguous")
+    cache = paged_from_golden(g)
+    with pytest.raises(RuntimeError):
+        f.paged_quant_attention_cuda(torch.zeros(3, 4, 128, dtype=torch.float16), cache)
+    with pytest.raises(ValueError):
+        f.paged_quant_attention_cuda(dev(g["q"])[:2], cache)
+    with pytest.raises(ValueError):
+        f.paged_quant_attention_cuda(dev(g["q"])[:, :3], cache)  # 3 q heads over 4 kv heads
+
+
+# ---------------------------------------------------------------------------------
+# append / allocator
+# ---------------------------------------------------------------------------------
+
+
+def test_functional_cache_append_bit_exact():
+    g = load_golden("cache_append")
+    f = fs()
+    c0 = f.PagedKVCache(qt_dev(g, "kq0"), qt_dev(g, "vq0"), dev(g["table0"]), dev(g["lengths0"]), 16, 7)
+    c1 = c0.append(dev(g["k_new"]), dev(g["v_new"]))
+    same_quant(c1.k_quant, g.quant("kq1"))
+    same_quant(c1.v_quant, g.quant("vq1"))
+    np.testing.assert_array_equal(c1.block_table.cpu().numpy(), g["table1"])
+    np.testing.assert_array_equal(c1.lengths.cpu().numpy(), g["lengths1"])
+    assert c1.max_seq_len == int(g["max_seq_len1"])
+
+
+class _DevTokens(dict):
+    def __getitem__(self, k):
+        v = dict.__getitem__(self, k)
+        return dev(v) if isinstance(v, np.ndarray) and k.startswith("tok.") else v
+
+
+def test_allocator_lifecycle_bit_exact():
+    from test_oracle_golden import replay_allocator
+
+    g = load_golden("allocator_lifecycle")
+    f = fs()
+    a = f.PagedKVAllocator(capacity_blocks=int(g["capacity"]), heads=int(g["heads"]), head_dim=int(g["head_dim"]),
+                           block_size=int(g["block_size"]), device="cuda")
+    replay_allocator(_DevTokens(g), a)
+    same_quant(a.k_quant, g.quant("kq"))
+    same_quant(a.v_quant, g.quant("vq"))
+    assert a.free_blocks == [int(x) for x in g["free_blocks"]]
+    cache = a.to_cache([30, 40, 50])
+    np.testing.assert_array_equal(cache.block_table.cpu().numpy(), g["table"])
+    np.testing.assert_array_equal(cache.lengths.cpu().numpy(), g["lengths"])
+    st = a.stats()
+    for k, v in zip(g["stats_keys"], g["stats_vals"]):
+        assert st[str(k)] == pytest.approx(float(v), abs=0, rel=1e-12)
+    # H=2, D=128: attention over the allocator's cache
+    out = f.paged_quant_attention_cuda(dev(g["q"]), cache)
+    close(out, g["out"])
+
+
+def test_allocator_random_decode_loop_matches_oracle():
+    rng = np.random.default_rng(11)
+    f = fs()
+    H, D, cap = 4, 128, 64
+    ga = f.PagedKVAllocator(capacity_blocks=cap, heads=H, head_dim=D, device="cuda")
+    oa = O.OAllocator(cap, H, D)
+    live = []
+    nxt = 0
+    for step in range(60):
+        if len(live) < 5 and rng.random() < 0.5:
+            n = int(rng.integers(1, 70))
+            k = rng.standard_normal((1, H, n, D)).astype(np.float16)
+            v = rng.standard_normal((1, H, n, D)).astype(np.float16)
+            if len(oa.free_blocks) >= (n + 15) // 16 + 8:
+                ga.add_request(nxt, dev(k), dev(v))
+                oa.add_request(nxt, k, v)
+                live.append(nxt)
+                nxt += 1
+        if live and len(oa.free_blocks) > 8:
+            t = int(rng.integers(1, 3))
+            k = rng.standard_normal((len(live), H, t, D)).astype(np.float16)
+            v = rng.standard_normal((len(live), H, t, D)).astype(np.float16)
+            ga.append_batch(live, dev(k), dev(v))
+            oa.append_batch(live, k, v)
+        if live and rng.random() < 0.2:
+            r = live.pop(int(rng.integers(0, len(live))))
+            ga.release_request(r)
+            oa.release_request(r)
+    same_quant(ga.k_quant, oa.k_quant)
+    same_quant(ga.v_quant, oa.v_quant)
+    assert ga.free_blocks == oa.free_blocks
+    if live:
+        q = rng.standard_normal((len(live), H, D)).astype(np.float16)
+        close(f.paged_quant_attention_cuda(dev(q), ga.to_cache(live)), O.paged_quant_attention(q, oa.to_cache(live)))
