@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 
 #include <math.h>
+#include <stdlib.h>
 #include <mutex>
 #include <stdint.h>
 
@@ -74,35 +75,40 @@ struct DecodeParams {
   float qk_scale_log2;
 };
 
-template <int kWarps, int kStages>
+// Shared-memory plan of one CTA: a ring of kNS page stages (K 2 KB + V 2 KB, 1024-byte
+// aligned for the 128-byte TMA swizzle), 32 bytes of qparams per stage
+// (k_scale, v_scale, k zero-point word, v zero-point word, flags), and a full / empty
+// mbarrier pair per stage.  The warp merge at the end reuses the ring.
+template <int kW, int kNS>
 struct SmemLayout {
-  static constexpr int kStageRegion = kWarps * kStages * kStageBytes;
-  static constexpr int kMetaRegion = kWarps * kStages * kMetaBytes;
-  static constexpr int kBarRegion = kWarps * kStages * 8;
-  static constexpr int kMergeBytes = kWarps * (2 * kMaxG + kMaxG * kD) * 4;
+  static constexpr int kStageRegion = kNS * kStageBytes;
+  static constexpr int kMetaRegion = kNS * kMetaBytes;
+  static constexpr int kBarRegion = kNS * 16;
+  static constexpr int kMergeBytes = kW * (2 * kMaxG + kMaxG * kD) * 4;
   static_assert(kMergeBytes <= kStageRegion, "merge scratch reuses the stage ring");
+  static_assert((kNS & (kNS - 1)) == 0, "stage count must be a power of two");
   static constexpr int kTotal = 1024 /*alignment slack*/ + kStageRegion + kMetaRegion + kBarRegion;
 };
 
-__device__ __forceinline__ uint32_t kv_to_f16x2(uint32_t x, uint32_t z2) {
-  // x holds bytes [b_lo, *, b_hi, *] (int8 storage of uint8-128).  Keep the low byte of
-  // each half, flip the sign bit (int8 -> uint8 = u) and insert exponent 0x64: the half
-  // is then exactly 1024 + u.  Subtracting 1024 + zp gives the exact integer u - zp.
-  uint32_t r;
-  asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(r) : "r"(x), "r"(0x00FF00FFu), "r"(0x64806480u));
-  // 0x6a = (a & b) ^ c
-  return hsub2_u32(r, z2);
-}
+constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent bytes: half 0x64xx == 1024 + xx
 
-template <bool kPaged, int kWarps, int kStages>
-__global__ void __launch_bounds__(kWarps * 32)
+// One CTA = one (request, kv head, split).  Warps 0..kW-1 consume pages; warp kW is the
+// producer that keeps the ring full with TMA tile loads and cp.async qparam copies.
+// kMode is a profiling aid: 0 = normal; 1 = consumers read the stage and release it but
+// skip the math; 2 = consumers only wait and release (pure data movement).
+template <bool kPaged, int kW, int kNS, int kMode>
+__global__ void __launch_bounds__((kW + 1) * 32, (kW <= 4 ? 3 : 2))
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeParams p) {
-  using L = SmemLayout<kWarps, kStages>;
+  using L = SmemLayout<kW, kNS>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
   const uint32_t base_s = (raw_s + 1023u) & ~1023u;
   uint8_t* base_p = smem_raw + (base_s - raw_s);
+  const uint32_t meta_s = base_s + L::kStageRegion;
+  uint32_t* meta_p = reinterpret_cast<uint32_t*>(base_p + L::kStageRegion);
+  const uint32_t full_s = base_s + L::kStageRegion + L::kMetaRegion;
+  const uint32_t empty_s = full_s + kNS * 8;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -110,299 +116,311 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int g = lane >> 2;
   const int c = lane & 3;
 
-  const uint32_t ring_s = base_s + warp * kStages * kStageBytes;
-  uint32_t* meta_p = reinterpret_cast<uint32_t*>(base_p + L::kStageRegion) + warp * kStages * (kMetaBytes / 4);
-  const uint32_t meta_s = base_s + L::kStageRegion + warp * kStages * kMetaBytes;
-  const uint32_t bar_s = base_s + L::kStageRegion + L::kMetaRegion + warp * kStages * 8;
-
   // ---- work item ------------------------------------------------------------
   const int S = p.S;
-  const int blk = blockIdx.x;
-  const int split = blk % S;
-  const int bh = blk / S;
+  const int split = blockIdx.x % S;
+  const int bh = blockIdx.x / S;
   const int h = bh % p.Hkv;
   const int b = bh / p.Hkv;
+  int64_t len64 = p.max_seq_len;
+  if (p.lengths != nullptr) len64 = min(len64, p.lengths[b]);
+  const int len = (int)max(len64, (int64_t)0);
+  int npages = (len + kPage - 1) / kPage;
+  npages = kPaged ? min(npages, p.cols) : (int)min((int64_t)npages, p.num_blocks);
+  const int len_eff = min(len, npages * kPage);
+  const int lo = (int)max(p.page_begin, (int64_t)0);
+  const int hi = p.page_end > 0 ? (int)min(p.page_end, (int64_t)npages) : npages;
+  const int span = hi > lo ? hi - lo : 0;
+  const int chunk = (span + S - 1) / S;
+  const int p0 = min(lo + split * chunk, max(hi, lo));
+  const int n = max(min(hi, p0 + chunk) - p0, 0);  // pages of this CTA
 
-  int64_t len = p.max_seq_len;
-  if (p.lengths != nullptr) len = min(len, p.lengths[b]);
-  if (len < 0) len = 0;
-  int64_t npages = (len + kPage - 1) / kPage;
-  npages = kPaged ? min(npages, (int64_t)p.cols) : min(npages, p.num_blocks);
-  const int64_t len_eff = min(len, npages * kPage);
-  const int64_t lo = max(p.page_begin, (int64_t)0);
-  const int64_t hi = p.page_end > 0 ? min(p.page_end, npages) : npages;
-  const int64_t span = hi > lo ? hi - lo : 0;
-  const int64_t chunk = (span + S - 1) / S;
-  const int64_t p0 = lo + (int64_t)split * chunk;
-  const int64_t p1 = min(hi, p0 + chunk);
-  const int nj = (p1 - p0 > warp) ? (int)((p1 - p0 - warp + kWarps - 1) / kWarps) : 0;
-
-  if (lane == 0) {
-    for (int st = 0; st < kStages; ++st) mbar_init(bar_s + 8 * st, 2);
+  if (tid == 0) {
+    for (int st = 0; st < kNS; ++st) {
+      mbar_init(full_s + 8 * st, 2);
+      mbar_init(empty_s + 8 * st, 1);
+    }
     fence_mbar_init();
     fence_proxy_async_smem();
   }
-  if (tid == 0) {
-    prefetch_tmap(&tmk);
-    prefetch_tmap(&tmv);
-  }
-  __syncwarp();
+  __syncthreads();
 
-  // ---- query fragment: thread (g,c) holds q[g][32c .. 32c+32) -----------------
-  uint32_t qh[16];
-  if (g < p.G) {
-    const uint4* qp = reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.Hq + (size_t)h * p.G + g) * kD + 32 * c);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 v = __ldg(qp + i);
-      qh[4 * i + 0] = v.x;
-      qh[4 * i + 1] = v.y;
-      qh[4 * i + 2] = v.z;
-      qh[4 * i + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) qh[i] = 0u;
-  }
-
-  // ---- page-id window (paged) ---------------------------------------------------
-  const int64_t* trow = kPaged ? p.table + (size_t)b * p.cols : nullptr;
-  auto tbl_load = [&](int jj) -> long long {
-    if (!kPaged || jj >= nj) return -1;
-    return (long long)trow[p0 + warp + (int64_t)jj * kWarps];
-  };
-  long long tcur = tbl_load(lane);
-  long long tnxt = tbl_load(32 + lane);
-  int wbase = 0;
-  const uint64_t policy = l2_policy_evict_first();
-
-  auto issue = [&](int j) {  // warp-uniform
-    long long phys;
-    if (kPaged) {
-      if (j >= wbase + 32) {
-        tcur = tnxt;
-        tnxt = tbl_load(wbase + 64 + lane);
-        wbase += 32;
-      }
-      phys = __shfl_sync(0xffffffffu, tcur, j - wbase);
-    } else {
-      phys = p0 + warp + (int64_t)j * kWarps;
-    }
-    if (lane == 0) {
-      const int st = j % kStages;
-      const uint32_t bar = bar_s + 8 * st;
-      uint32_t* m = meta_p + st * (kMetaBytes / 4);
-      const bool ok = !kPaged || (phys >= 0 && phys < p.num_blocks);
-      if (!ok) {
-        if (phys >= p.num_blocks && p.status != nullptr) atomicOr(p.status, FS_DEV_BAD_PAGE);
-        m[4] = 0u;
-        mbar_arrive(bar);
-        mbar_arrive(bar);
-      } else {
-        const int64_t e = kPaged ? phys * p.Hkv + h : ((int64_t)b * p.Hkv + h) * p.num_blocks + phys;
-        const int32_t row = (int32_t)(e * kPage);
-        uint32_t flags = 1u;
-        const bool word_ok = (e | 1) < p.zp_count;
-        if (word_ok) {
-          flags |= (uint32_t)(e & 1) << 1;
-        } else {
-          m[2] = (uint32_t)(uint16_t)p.k_zero[e];
-          m[3] = (uint32_t)(uint16_t)p.v_zero[e];
-        }
-        m[4] = flags;
-        mbar_arrive_expect_tx(bar, kStageBytes);
-        const uint32_t dst = ring_s + st * kStageBytes;
-        tma_load_2d(dst, &tmk, 0, row, bar, policy);
-        tma_load_2d(dst + kPageBytes, &tmv, 0, row, bar, policy);
-        const uint32_t ms = meta_s + st * kMetaBytes;
-        cp_async_4(ms + 0, p.k_scale + e);
-        cp_async_4(ms + 4, p.v_scale + e);
-        if (word_ok) {
-          cp_async_4(ms + 8, p.k_zero + (e & ~1ll));
-          cp_async_4(ms + 12, p.v_zero + (e & ~1ll));
-        }
-        cp_async_mbar_arrive_noinc(bar);
-      }
-    }
-  };
-
+  bool aborted = false;
   float acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[i][k] = 0.f;
-  float m_run = -1.0e30f;  // running max (log2 domain), finite so exp2 never sees inf-inf
-  float l_run = 0.f;       // this thread's partial of the softmax denominator
-  int j_done = 0;
-  bool aborted = false;
+  float m_run = -1.0e30f;  // running max (log2 domain); finite so exp2 never sees inf-inf
+  float l_run = 0.f;       // this thread's share of the softmax denominator
 
-  const int npre = nj < kStages ? nj : kStages;
-  for (int j = 0; j < npre; ++j) issue(j);
-
-  for (int j = 0; j < nj; ++j) {
-    const int st = j % kStages;
-    if (!mbar_wait_bounded(bar_s + 8 * st, (uint32_t)((j / kStages) & 1), kTimeoutNs)) {
-      aborted = true;
-      j_done = j;
-      if (lane == 0 && p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
-      break;
+  if (warp == kW) {
+    // ============================ producer warp ===============================
+    // Pages are issued in batches of kIssue: lane j handles page i + j, so one warp
+    // instruction issues kIssue TMA loads.
+    constexpr int kIssue = 8;
+    static_assert(kNS % kIssue == 0 && 32 % kIssue == 0, "issue batch must divide the ring");
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+    const uint64_t policy = l2_policy_evict_first();
+    const int64_t* trow = kPaged ? p.table + (size_t)b * p.cols + p0 : nullptr;
+    long long tcur = (kPaged && lane < n) ? (long long)trow[lane] : -1;
+    long long tnxt = (kPaged && 32 + lane < n) ? (long long)trow[32 + lane] : -1;
+    const int64_t ebase = kPaged ? (int64_t)h : ((int64_t)b * p.Hkv + h) * p.num_blocks;
+    for (int i0 = 0; i0 < n; i0 += kIssue) {
+      long long phys;
+      if (kPaged) {
+        if ((i0 & 31) == 0 && i0 > 0) {
+          tcur = tnxt;
+          tnxt = (i0 + 32 + lane < n) ? (long long)trow[i0 + 32 + lane] : -1;
+        }
+        phys = __shfl_sync(0xffffffffu, tcur, (i0 + (lane & (kIssue - 1))) & 31);
+      } else {
+        phys = p0 + i0 + lane;
+      }
+      const int i = i0 + lane;
+      if (lane < kIssue && i < n) {
+        const int st = i & (kNS - 1);
+        const uint32_t full = full_s + 8 * st;
+        if (i >= kNS && !mbar_wait_bounded(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kTimeoutNs)) {
+          if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
+          aborted = true;
+        }
+        if (!aborted) {
+          uint32_t* m = meta_p + st * (kMetaBytes / 4);
+          const bool ok = !kPaged || (phys >= 0 && phys < p.num_blocks);
+          if (!ok) {
+            if (phys >= p.num_blocks && p.status != nullptr) atomicOr(p.status, FS_DEV_BAD_PAGE);
+            m[4] = 0u;
+            mbar_arrive(full);
+            mbar_arrive(full);
+          } else {
+            const int64_t e = kPaged ? phys * p.Hkv + ebase : ebase + phys;
+            const bool word_ok = (e | 1) < p.zp_count;
+            if (!word_ok) {  // last element of an odd-sized zero-point array: plain loads
+              m[2] = (uint32_t)(uint16_t)p.k_zero[e];
+              m[3] = (uint32_t)(uint16_t)p.v_zero[e];
+            }
+            m[4] = 1u | (word_ok ? ((uint32_t)(e & 1) << 1) : 0u);
+            mbar_arrive_expect_tx(full, kStageBytes);
+            const uint32_t dst = base_s + st * kStageBytes;
+            tma_load_2d(dst, &tmk, 0, (int32_t)(e * kPage), full, policy);
+            tma_load_2d(dst + kPageBytes, &tmv, 0, (int32_t)(e * kPage), full, policy);
+            const uint32_t ms = meta_s + st * kMetaBytes;
+            cp_async_4(ms + 0, p.k_scale + e);
+            cp_async_4(ms + 4, p.v_scale + e);
+            if (word_ok) {
+              cp_async_4(ms + 8, p.k_zero + (e & ~1ll));
+              cp_async_4(ms + 12, p.v_zero + (e & ~1ll));
+            }
+            cp_async_mbar_arrive_noinc(full);
+          }
+        }
+      }
+      if (__any_sync(0xffffffffu, aborted)) {
+        aborted = true;
+        break;
+      }
     }
-    const volatile uint32_t* m = meta_p + st * (kMetaBytes / 4);
-    const uint32_t flags = m[4];
-    const int64_t lpage = p0 + warp + (int64_t)j * kWarps;
-    if (!(flags & 1u)) {  // unallocated / rejected page: masked like the reference
+  } else {
+    // ============================ consumer warps ===============================
+    // query fragment: thread (g,c) holds q[g][32c .. 32c+32) as the A operand of
+    // S = Q K^T, where logical k (2c, 2c+1 | 2c+8, 2c+9) of step j is head dim
+    // 32c+4j+(0,1 | 2,3).  qsum = sum of the same fp16 values (row g).
+    uint32_t qh[16];
+    float qsum = 0.f;
+    if (g < p.G) {
+      const uint4* qp =
+          reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.Hq + (size_t)h * p.G + g) * kD + 32 * c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = __ldg(qp + i);
+        qh[4 * i + 0] = v.x;
+        qh[4 * i + 1] = v.y;
+        qh[4 * i + 2] = v.z;
+        qh[4 * i + 3] = v.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&qh[i]));
+        qsum += f2.x + f2.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qh[i] = 0u;
+    }
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+
+    // per-thread offsets inside a stage (128-byte swizzle: the 16-byte chunk index of
+    // row r is XOR-ed with r & 7).  K: rows g and g+8, chunks 2c and 2c+1.
+    uint32_t koff[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) koff[nt][e2] = (g + 8 * nt) * 128 + (((2 * c + e2) ^ g) << 4);
+    // V: ldmatrix.x4.trans #k reads 8x8 b16 matrices (chunk 2k | 2k+1) x (tokens 0-7 | 8-15);
+    // lane l supplies row (l & 7) of matrix (l >> 3).
+    uint32_t voff[4];
+    {
+      const int mat = lane >> 3, r = lane & 7;
+      const int tok = 8 * (mat & 1) + r;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) voff[k] = kPageBytes + tok * 128 + (((2 * k + (mat >> 1)) ^ r) << 4);
+    }
+
+    for (int i = warp; i < n; i += kW) {
+      const int st = i & (kNS - 1);
+      if (!mbar_wait_bounded(full_s + 8 * st, (uint32_t)((i / kNS) & 1), kTimeoutNs)) {
+        if (lane == 0 && p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
+        aborted = true;
+        break;
+      }
+      const volatile uint32_t* m = meta_p + st * (kMetaBytes / 4);
+      const uint32_t flags = m[4];
+      if (!(flags & 1u)) {  // unallocated / rejected page: masked like the reference
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_s + 8 * st);
+        continue;
+      }
+      const float ks = __uint_as_float(m[0]);
+      const float vs = __uint_as_float(m[1]);
+      const uint32_t sh = (flags & 2u) ? 16u : 0u;
+      const uint32_t kz = (m[2] >> sh) & 0xffffu;
+      const uint32_t vz = (m[3] >> sh) & 0xffffu;
+      if (kMode == 2) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_s + 8 * st);
+        continue;
+      }
+      const uint32_t sbase = base_s + st * kStageBytes;
+      uint4 kr[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sbase + koff[nt][e2]);
+      uint32_t vr[16];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        ldsm_x4_trans(sbase + voff[k], vr[4 * k], vr[4 * k + 1], vr[4 * k + 2], vr[4 * k + 3]);
       __syncwarp();
-      if (j + kStages < nj) issue(j + kStages);
-      continue;
-    }
-    const float ks = __uint_as_float(m[0]);
-    const float vs = __uint_as_float(m[1]);
-    const uint32_t hi_half = flags & 2u;
-    const uint32_t kz = hi_half ? (m[2] >> 16) : (m[2] & 0xffffu);
-    const uint32_t vz = hi_half ? (m[3] >> 16) : (m[3] & 0xffffu);
+      if (lane == 0) mbar_arrive(empty_s + 8 * st);  // stage may be refilled now
+      if (kMode == 1) {
+        acc[0][0] += __uint_as_float((kr[0][0].x ^ kr[1][1].w ^ vr[0] ^ vr[15]) & 0x007fffffu);
+        continue;
+      }
 
-    const uint32_t sk = ring_s + st * kStageBytes;
-    const uint32_t sv = sk + kPageBytes;
-    uint4 kr[2][2];
+      // ---- S = Q K^T: K bytes become 1024+u exactly (sign flip + exponent bytes);
+      // the (1024 + zp) offset is removed per page with qsum -------------------------
+      float sa[2][2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int r = g + 8 * nt;
+      for (int a = 0; a < 2; ++a)
 #pragma unroll
-      for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sk + r * 128 + (((2 * c + e2) ^ (r & 7)) << 4));
-    }
-    uint4 vr[4];
+        for (int bb = 0; bb < 2; ++bb)
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r = 2 * c + (t & 1) + 8 * (t >> 1);
-      vr[t] = lds128(sv + r * 128 + ((g ^ (r & 7)) << 4));
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (j + kStages < nj) issue(j + kStages);
+          for (int k = 0; k < 4; ++k) sa[a][bb][k] = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint4 kv = kr[nt][jj >> 2];
+          const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
+          const uint32_t x = w ^ 0x80808080u;
+          mma_16816(sa[nt][jj & 1], qh[2 * jj], 0u, qh[2 * jj + 1], 0u, prmt(x, kMagic, 0x5140u),
+                    prmt(x, kMagic, 0x5342u));
+        }
+      }
+      const float f = ks * p.qk_scale_log2;
+      const float zq = -(1024.0f + (float)kz) * qsum;
+      float t[4];
+      t[0] = fmaf(1.f, sa[0][0][0] + sa[0][1][0], zq) * f;  // token 2c
+      t[1] = fmaf(1.f, sa[0][0][1] + sa[0][1][1], zq) * f;  // token 2c+1
+      t[2] = fmaf(1.f, sa[1][0][0] + sa[1][1][0], zq) * f;  // token 8+2c
+      t[3] = fmaf(1.f, sa[1][0][1] + sa[1][1][1], zq) * f;  // token 9+2c
+      const int pos0 = (p0 + i) * kPage;
+      if (pos0 + kPage > len_eff) {
+        if (pos0 + 2 * c >= len_eff) t[0] = -INFINITY;
+        if (pos0 + 2 * c + 1 >= len_eff) t[1] = -INFINITY;
+        if (pos0 + 8 + 2 * c >= len_eff) t[2] = -INFINITY;
+        if (pos0 + 9 + 2 * c >= len_eff) t[3] = -INFINITY;
+      }
+      float mx = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (__any_sync(0xffffffffu, mx > m_run)) {
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = ex2_approx(m_run - m_new);
+        m_run = m_new;
+        l_run *= alpha;
+        const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
+        const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+#pragma unroll
+        for (int i2 = 0; i2 < 8; ++i2) {
+          acc[i2][0] *= a0;
+          acc[i2][1] *= a1;
+          acc[i2][2] *= a0;
+          acc[i2][3] *= a1;
+        }
+      }
+      float pr[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pr[k] = ex2_approx(t[k] - m_run);
+      l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
+      const uint32_t pb0 = pack_half2(pr[0] * vs, pr[1] * vs);
+      const uint32_t pb1 = pack_half2(pr[2] * vs, pr[3] * vs);
 
-    // ---- S = Q K^T (fp16 MMA, exact centred K) --------------------------------
-    const uint32_t zk2 = (0x6400u + (kz & 0x1ffu)) * 0x10001u;
-    const uint32_t zv2 = (0x6400u + (vz & 0x1ffu)) * 0x10001u;
-    float sa[2][2][4];
+      // ---- O += P V: vr(chunk i, tokens 0-7 | 8-15) hold bytes
+      // [V[2c][d], V[2c][d+1], V[2c+1][d], V[2c+1][d+1]] with d = 16i + 2g ------------
+      const uint32_t zv2 = (0x6400u + vz) * 0x10001u;
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int bb = 0; bb < 2; ++bb)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) sa[a][bb][k] = 0.f;
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const uint4 kv = kr[nt][jj >> 2];
-        const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
-        const uint32_t x = w ^ 0x80808080u;
-        const uint32_t b0 = hsub2_u32(prmt(x, 0x64646464u, 0x5140u), zk2);
-        const uint32_t b1 = hsub2_u32(prmt(x, 0x64646464u, 0x5342u), zk2);
-        mma_16816(sa[nt][jj & 1], qh[2 * jj], 0u, qh[2 * jj + 1], 0u, b0, b1);
+      for (int i2 = 0; i2 < 8; ++i2) {
+        const uint32_t x0 = vr[4 * (i2 >> 1) + 2 * (i2 & 1)] ^ 0x80808080u;
+        const uint32_t x1 = vr[4 * (i2 >> 1) + 2 * (i2 & 1) + 1] ^ 0x80808080u;
+        mma_16816(acc[i2], hsub2_u32(prmt(x0, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x0, kMagic, 0x5341u), zv2),
+                  hsub2_u32(prmt(x1, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x1, kMagic, 0x5341u), zv2), pb0, pb1);
       }
     }
-    const float f = ks * p.qk_scale_log2;
-    float t[4];
-    t[0] = (sa[0][0][0] + sa[0][1][0]) * f;  // token 2c
-    t[1] = (sa[0][0][1] + sa[0][1][1]) * f;  // token 2c+1
-    t[2] = (sa[1][0][0] + sa[1][1][0]) * f;  // token 8+2c
-    t[3] = (sa[1][0][1] + sa[1][1][1]) * f;  // token 9+2c
-    const int64_t pos0 = lpage * kPage;
-    if (pos0 + kPage > len_eff) {
-      const int tok[4] = {2 * c, 2 * c + 1, 8 + 2 * c, 9 + 2 * c};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (pos0 + tok[i] >= len_eff) t[i] = -INFINITY;
-    }
-    float mx = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    if (__any_sync(0xffffffffu, mx > m_run)) {
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = exp2f(m_run - m_new);
-      m_run = m_new;
-      l_run *= alpha;
-      const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
-      const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        acc[i][0] *= a0;
-        acc[i][1] *= a1;
-        acc[i][2] *= a0;
-        acc[i][3] *= a1;
-      }
-    }
-    float pr[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) pr[i] = exp2f(t[i] - m_run);
-    l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
-    const uint32_t pb0 = pack_half2(pr[0] * vs, pr[1] * vs);
-    const uint32_t pb1 = pack_half2(pr[2] * vs, pr[3] * vs);
-
-    // ---- O += P V (fp16 MMA, exact centred V) ---------------------------------
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int w = i >> 1;
-      const uint32_t k0 = 2u * (i & 1);
-      const uint32_t sel_a = k0 | (k0 << 4) | ((4u + k0) << 8) | ((4u + k0) << 12);
-      const uint32_t sel_b = (k0 + 1u) | ((k0 + 1u) << 4) | ((5u + k0) << 8) | ((5u + k0) << 12);
-      const uint32_t w0 = w == 0 ? vr[0].x : w == 1 ? vr[0].y : w == 2 ? vr[0].z : vr[0].w;
-      const uint32_t w1 = w == 0 ? vr[1].x : w == 1 ? vr[1].y : w == 2 ? vr[1].z : vr[1].w;
-      const uint32_t w2 = w == 0 ? vr[2].x : w == 1 ? vr[2].y : w == 2 ? vr[2].z : vr[2].w;
-      const uint32_t w3 = w == 0 ? vr[3].x : w == 1 ? vr[3].y : w == 2 ? vr[3].z : vr[3].w;
-      const uint32_t a0 = kv_to_f16x2(prmt(w0, w1, sel_a), zv2);
-      const uint32_t a1 = kv_to_f16x2(prmt(w0, w1, sel_b), zv2);
-      const uint32_t a2 = kv_to_f16x2(prmt(w2, w3, sel_a), zv2);
-      const uint32_t a3 = kv_to_f16x2(prmt(w2, w3, sel_b), zv2);
-      mma_16816(acc[i], a0, a1, a2, a3, pb0, pb1);
-    }
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
   }
 
-  if (aborted) {  // drain our own copies in flight (bounded) before the ring is reused
-    const int jmax = min(nj, j_done + kStages);
-    for (int j = j_done; j < jmax; ++j)
-      (void)mbar_wait_bounded(bar_s + 8 * (j % kStages), (uint32_t)((j / kStages) & 1), kTimeoutNs / 16);
-  }
-
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-
-  // ---- merge the warps of this CTA through shared memory ------------------------
-  __syncthreads();  // every warp is done with its ring
+  // ---- merge the consumer warps through shared memory ---------------------------
+  __syncthreads();  // every page has been consumed, so no copy still targets the ring
+  const bool any_abort = __syncthreads_or(aborted ? 1 : 0);
+  if (any_abort) return;  // status word carries FS_DEV_TIMEOUT; outputs are not written
   float* ms = reinterpret_cast<float*>(base_p);
-  float* ls = ms + kWarps * kMaxG;
-  float* accs = ls + kWarps * kMaxG;  // [kWarps][kMaxG][kD]
-  if (c == 0) {
-    ms[warp * kMaxG + g] = m_run;
-    ls[warp * kMaxG + g] = l_run;
-  }
+  float* ls = ms + kW * kMaxG;
+  float* accs = ls + kW * kMaxG;  // [kW][kMaxG][kD]
+  if (warp < kW) {
+    if (c == 0) {
+      ms[warp * kMaxG + g] = m_run;
+      ls[warp * kMaxG + g] = l_run;
+    }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int d = 16 * g + 2 * i;
-    float* a0p = accs + (warp * kMaxG + 2 * c) * kD;
-    float* a1p = accs + (warp * kMaxG + 2 * c + 1) * kD;
-    a0p[d] = acc[i][0];
-    a1p[d] = acc[i][1];
-    a0p[d + 1] = acc[i][2];
-    a1p[d + 1] = acc[i][3];
+    for (int i2 = 0; i2 < 8; ++i2) {
+      const int d = 16 * i2 + 2 * g;
+      float* a0p = accs + (warp * kMaxG + 2 * c) * kD;
+      float* a1p = accs + (warp * kMaxG + 2 * c + 1) * kD;
+      a0p[d] = acc[i2][0];
+      a1p[d] = acc[i2][1];
+      a0p[d + 1] = acc[i2][2];
+      a1p[d + 1] = acc[i2][3];
+    }
   }
   __syncthreads();
 
-  const bool any_abort = __syncthreads_or(aborted ? 1 : 0);
-  if (any_abort) return;  // status word carries FS_DEV_TIMEOUT; outputs are not written
-
+  constexpr int kThreads = (kW + 1) * 32;
   const int nout = p.G * kD;
   const float kLn2 = 0.6931471805599453f;
-  for (int idx = tid; idx < nout; idx += kWarps * 32) {
+  for (int idx = tid; idx < nout; idx += kThreads) {
     const int qg = idx >> 7;
     const int d = idx & (kD - 1);
     float M = -1.0e30f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ms[w * kMaxG + qg]);
+    for (int w = 0; w < kW; ++w) M = fmaxf(M, ms[w * kMaxG + qg]);
     float Lsum = 0.f, O = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < kW; ++w) {
       const float sc = exp2f(ms[w * kMaxG + qg] - M);
       Lsum += ls[w * kMaxG + qg] * sc;
       O += accs[(w * kMaxG + qg) * kD + d] * sc;
@@ -436,7 +454,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  for (int idx = tid; idx < nout; idx += kWarps * 32) {
+  for (int idx = tid; idx < nout; idx += kThreads) {
     const int qg = idx >> 7;
     const int d = idx & (kD - 1);
     const size_t prow0 = (size_t)bh * S * p.G + qg;
@@ -468,8 +486,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 // host side
 // ---------------------------------------------------------------------------------
 
-constexpr int kWarpsCfg = 4;
-constexpr int kStagesCfg = 4;
+constexpr int kWarpsCfg = 4;    // consumer warps per CTA
+constexpr int kStagesCfg = 16;  // ring stages per CTA
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -502,6 +520,25 @@ static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
   return r == CUDA_SUCCESS ? FS_OK : FS_ERR_CUDA;
 }
 
+using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
+
+// FLASHSPEC_DEBUG_MODE (profiling only, results are wrong when set): 1 = skip the math,
+// 2 = data movement only.
+static int debug_mode() {
+  const char* v = getenv("FLASHSPEC_DEBUG_MODE");
+  const int m = v ? atoi(v) : 0;
+  return (m == 1 || m == 2) ? m : 0;
+}
+
+template <bool kPaged>
+static DecodeKernelFn kernel_for(int mode) {
+  switch (mode) {
+    case 1: return decode_kernel<kPaged, kWarpsCfg, kStagesCfg, 1>;
+    case 2: return decode_kernel<kPaged, kWarpsCfg, kStagesCfg, 2>;
+    default: return decode_kernel<kPaged, kWarpsCfg, kStagesCfg, 0>;
+  }
+}
+
 template <bool kPaged>
 static int configure_kernel(int device) {
   static bool done[2][kMaxDevices] = {};
@@ -510,9 +547,10 @@ static int configure_kernel(int device) {
   if (device < 0 || device >= kMaxDevices) return FS_ERR_CUDA;
   if (done[kPaged][device]) return FS_OK;
   using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel<kPaged, kWarpsCfg, kStagesCfg>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kTotal);
-  if (e != cudaSuccess) return FS_ERR_CUDA;
+  for (int mode = 0; mode < 3; ++mode)
+    if (cudaFuncSetAttribute(kernel_for<kPaged>(mode), cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kTotal) !=
+        cudaSuccess)
+      return FS_ERR_CUDA;
   done[kPaged][device] = true;
   return FS_OK;
 }
@@ -520,12 +558,14 @@ static int configure_kernel(int device) {
 static int resident_ctas(int device) {
   static int cached[kMaxDevices] = {};
   static std::mutex mu;
+  // the occupancy query needs the kernel's dynamic shared-memory limit raised first
+  if (configure_kernel<true>(device) != FS_OK) return device_sm_count(device);
   std::lock_guard<std::mutex> lock(mu);
   if (cached[device] > 0) return cached[device];
   int per_sm = 0;
   using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel<true, kWarpsCfg, kStagesCfg>,
-                                                    kWarpsCfg * 32, Lay::kTotal) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for<true>(0),
+                                                    (kWarpsCfg + 1) * 32, Lay::kTotal) != cudaSuccess ||
       per_sm <= 0)
     per_sm = 1;
   cached[device] = per_sm * device_sm_count(device);
@@ -649,8 +689,8 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
   const int64_t grid = (int64_t)a->batch * a->kv_heads * splits;
   if (grid >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
-  decode_kernel<kPaged, kWarpsCfg, kStagesCfg><<<(unsigned)grid, kWarpsCfg * 32, Lay::kTotal,
-                                                 reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
+  kernel_for<kPaged>(debug_mode())<<<(unsigned)grid, (kWarpsCfg + 1) * 32, Lay::kTotal,
+                                     reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
   return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
 }
 
