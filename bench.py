@@ -1,0 +1,403 @@
+"""Benchmark of the paged INT8 decode-attention hot path (driver contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg1]
+
+A step is one decode-attention call over the configuration's whole batch.  The
+default workload is BASELINE configs[1] (cfg1): paged INT8 KV, B16, 32 Q/KV heads,
+D128, seq 4096, page 16, pool = 4096 pages + 10% slack, shuffled block_table.
+Inputs are larger than L2 (539 MB of KV), so no flush is needed between steps.
+
+ours (default): KV pool, q and the table are resident in HBM; K timed steps of
+``paged_quant_attention_cuda`` between CUDA events (barrier + synchronize on both
+sides; N>1 = independent per-rank shards, max time over ranks).  ``value`` is the
+aggregate algorithmic bandwidth (bytes every rank's calls must move / time).
+``e2e`` times the same public call with the per-step inputs (q, block_table,
+lengths) copied from pinned host memory and the output copied back, every step.
+``roofline`` divides the kernel's achieved bytes/s (per-launch CUDA events) by the
+measured HBM copy peak.  ``cpu_baseline`` times the CPU oracle (a numpy port of
+the reference's ``paged_quant_attention``) on a bounded sample of the same data.
+
+reference: times that CPU port on the box's host cores over a bounded sample per
+step (rank 0 only under torchrun) and reports the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode-attn µs/call & achieved HBM TB/s (frac of B200 peak), paged INT8 KV"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["cfg1", "cfg2", "cfg3"], default="cfg1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-soak", action="store_true", help="skip the 1.5 s clock soak (for profiler launch lists)")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------
+# helpers
+# ------------------------------------------------------------------------------------
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_launch(config: str):
+    """Per-launch DRAM bytes (read + write) of the decode kernel from the committed ncu
+    summary, or None."""
+    p = ROOT / "profiles" / "traffic_per_launch.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == config:
+            return int(float(parts[1]))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU is busy."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float, gpu_index=None):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        window = [l for (t, l) in self.lines if t0 <= t <= t1] or [l for (_, l) in self.lines]
+        for line in window:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            if gpu_index is not None and f[0] != str(gpu_index):
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def build_workload(config: str, rank: int):
+    from flashspec_b200 import configs
+
+    seed = 1000 * rank
+    if config == "cfg1":
+        return configs.cfg1(seed=seed)
+    if config == "cfg2":
+        return configs.cfg2(seed=seed)
+    return configs.cfg3(seed=seed)
+
+
+# ------------------------------------------------------------------------------------
+# CPU baseline: numpy port of the reference paged path on a bounded sample
+# ------------------------------------------------------------------------------------
+
+
+def cpu_sample(wl, n_req: int):
+    """Host copy of the first n_req requests of the workload: their pages only, as an
+    oracle cache (the reference dequantizes the whole pool it is given)."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import flashspec_oracle as O
+
+    table = wl.cache.block_table[:n_req].cpu().numpy()
+    used = np.unique(table[table >= 0])
+    remap = np.full(int(used.max()) + 1, -1, np.int64)
+    remap[used] = np.arange(used.size)
+    import torch
+
+    idx = torch.from_numpy(used).to(wl.cache.k_quant.values.device)
+
+    def sub(qt):
+        return O.OQuant(qt.values[idx].cpu().numpy(), qt.scale[idx].cpu().numpy(), qt.zero_point[idx].cpu().numpy(),
+                        16, (used.size,) + tuple(qt.original_shape[1:]))
+
+    t = np.where(table >= 0, remap[np.maximum(table, 0)], -1)
+    lengths = np.array(wl.lengths[:n_req], np.int64)
+    cache = O.OPagedCache(sub(wl.cache.k_quant), sub(wl.cache.v_quant), t, lengths, 16, int(lengths.max()))
+    q = wl.q[:n_req].cpu().numpy()
+    return O, q, cache
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return 1
+
+
+def time_cpu_baseline(wl, n_req: int, reps: int):
+    O, q, cache = cpu_sample(wl, n_req)
+    O.paged_quant_attention(q, cache)  # warm-up
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.paged_quant_attention(q, cache)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    frac = sum((n + 15) // 16 for n in wl.lengths[:n_req]) / sum((n + 15) // 16 for n in wl.lengths)
+    full_s = t / frac  # the sample's share of the call's pages
+    return full_s, ts
+
+
+# ------------------------------------------------------------------------------------
+# arms
+# ------------------------------------------------------------------------------------
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    import torch  # noqa: F401  (device-free)
+
+    os.environ.setdefault("CUDA_VISIBLE_DEVICES", os.environ.get("CUDA_VISIBLE_DEVICES", ""))
+    wl = build_workload(args.config, 0)
+    n_req = 2 if args.config != "cfg3" else 1
+    steps = max(1, min(args.steps, 5))
+    warm = max(0, min(args.warmup, 1))
+    O, q, cache = cpu_sample(wl, n_req)
+    for _ in range(warm):
+        O.paged_quant_attention(q, cache)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        O.paged_quant_attention(q, cache)
+        ts.append(time.perf_counter() - t0)
+    frac = sum((n + 15) // 16 for n in wl.lengths[:n_req]) / sum((n + 15) // 16 for n in wl.lengths)
+    per_call = statistics.median(ts) / frac
+    value = wl.bytes_per_call / per_call / 1e12
+    sample = (f"first {n_req} of {len(wl.lengths)} requests of {wl.name} (their pages only), median of {steps} "
+              f"calls, scaled by page share {frac:.4f}")
+    cores = cpu_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus, "steps": steps,
+        "warmup": warm, "ms_per_step": per_call * 1e3, "us_per_call": per_call * 1e6, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 KV / fp32 accumulate", "data": "synthetic",
+        "config": {"workload": wl.name, "global_batch": len(wl.lengths), "seq_len": max(wl.lengths),
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    import flashspec_b200 as fs
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    wl = build_workload(args.config, rank)
+    q, cache = wl.q, wl.cache
+    splits = wl.num_splits
+
+    def call():
+        return fs.paged_quant_attention_cuda(q, cache, num_splits=splits)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # warm-up (W steps) and a clock soak of ~1.5 s so nvidia-smi sees the load
+    sampler = ClockSampler() if rank == 0 else None
+    for _ in range(max(3, args.warmup)):
+        call()
+    torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.start()
+    t_soak = time.time()
+    while not args.no_soak and time.time() - t_soak < 1.5:
+        for _ in range(200):
+            call()
+        torch.cuda.synchronize()
+
+    # ---- device-resident timed region ------------------------------------------------
+    stream = torch.cuda.current_stream(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    t_wall0 = time.time()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(args.steps):
+        evs[i][0].record(stream)
+        call()
+        evs[i][1].record(stream)
+    end.record(stream)
+    barrier()
+    t_wall1 = time.time()
+    elapsed_ms = start.elapsed_time(end)
+    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+
+    # ---- end-to-end through the public API with host buffers ----------------------------
+    e2e_steps = max(1, min(args.steps, 500))
+    q_host = q.cpu().pin_memory()
+    table_host = cache.block_table.cpu().pin_memory()
+    lengths_host = cache.lengths.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_dev, table_dev, lengths_dev = torch.empty_like(q), torch.empty_like(cache.block_table), torch.empty_like(cache.lengths)
+    cache_e2e = fs.PagedKVCache(cache.k_quant, cache.v_quant, table_dev, lengths_dev, cache.block_size, cache.max_seq_len)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        table_dev.copy_(table_host, non_blocking=True)
+        lengths_dev.copy_(lengths_host, non_blocking=True)
+        out = fs.paged_quant_attention_cuda(q_dev, cache_e2e, num_splits=splits)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    h2d = q.numel() * q.element_size() + cache.block_table.numel() * 8 + cache.lengths.numel() * 8
+    d2h = q.numel() * q.element_size()
+    if sampler is not None:
+        sampler.stop()
+    if rank != 0:
+        return
+
+    peak, peak_kind = measured_peaks()
+    achieved_gbs = wl.bytes_per_call / (launch_ms * 1e-3) / 1e9
+    total_bytes = wl.bytes_per_call * world * args.steps
+    value = total_bytes / (elapsed_ms * 1e-3) / 1e12
+    e2e_value = wl.bytes_per_call * world * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    clocks = sampler.summary(t_soak, t_wall1) if sampler is not None else {}
+    line = {
+        "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": elapsed_ms / args.steps,
+        "us_per_call": elapsed_ms / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 KV, fp16 q/out, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": wl.name, "global_batch": len(wl.lengths) * world, "seq_len": max(wl.lengths),
+                   "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "page": 16,
+                   "parallelism": f"request-shard x{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (no flush)", "bytes_per_call_per_gpu": wl.bytes_per_call},
+        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
+                     "frac": achieved_gbs / peak, "traffic": traffic_per_launch(args.config),
+                     "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                     "kernel_us": launch_ms * 1e3},
+        "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "us_per_call": e2e_ms / e2e_steps * 1e3,
+                "api": "flashspec_b200.paged_quant_attention_cuda with q/table/lengths from pinned host"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        n_req = 2 if args.config != "cfg3" else 1
+        full_s, ts = time_cpu_baseline(wl, n_req, reps=3)
+        line["cpu_baseline"] = {
+            "value": wl.bytes_per_call / full_s / 1e12, "unit": "TB/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"first {n_req} requests of {wl.name} (their pages), median of 3 calls, scaled by page share",
+            "us_per_call": full_s * 1e6,
+        }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -87,6 +87,10 @@ struct SmemLayout {
   static constexpr int kMergeBytes = kW * (2 * kMaxG + kMaxG * kD) * 4;
   static_assert(kMergeBytes <= kStageRegion, "merge scratch reuses the stage ring");
   static_assert((kNS & (kNS - 1)) == 0, "stage count must be a power of two");
+  // Every stage must always be consumed by the same warp (page i -> warp i % kW, stage
+  // i % kNS).  Otherwise a warp can wait on a stage's full barrier a whole phase early
+  // and the parity test aliases with the previous phase.
+  static_assert(kNS % kW == 0, "stage count must be a multiple of the consumer warps");
   static constexpr int kTotal = 1024 /*alignment slack*/ + kStageRegion + kMetaRegion + kBarRegion;
 };
 
@@ -96,8 +100,8 @@ constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent bytes: half 0x64xx ==
 // producer that keeps the ring full with TMA tile loads and cp.async qparam copies.
 // kMode is a profiling aid: 0 = normal; 1 = consumers read the stage and release it but
 // skip the math; 2 = consumers only wait and release (pure data movement).
-template <bool kPaged, int kW, int kNS, int kMode>
-__global__ void __launch_bounds__((kW + 1) * 32, (kW <= 4 ? 3 : 2))
+template <bool kPaged, int kW, int kNS, int kMinBlocks, int kMode>
+__global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const DecodeParams p) {
   using L = SmemLayout<kW, kNS>;
@@ -294,11 +298,30 @@ __global__ void __launch_bounds__((kW + 1) * 32, (kW <= 4 ? 3 : 2))
         continue;
       }
       const uint32_t sbase = base_s + st * kStageBytes;
-      uint4 kr[2][2];
+      // ---- S = Q K^T: K bytes become 1024+u exactly (sign flip + exponent bytes);
+      // the (1024 + zp) offset is removed per page with qsum -------------------------
+      float sa[2][4];
+      {
+        uint4 kr[2][2];
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sbase + koff[nt][e2]);
+          for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sbase + koff[nt][e2]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) sa[nt][k] = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const uint4 kv = kr[nt][jj >> 2];
+            const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
+            const uint32_t x = w ^ 0x80808080u;
+            mma_16816(sa[nt], qh[2 * jj], 0u, qh[2 * jj + 1], 0u, prmt(x, kMagic, 0x5140u), prmt(x, kMagic, 0x5342u));
+          }
+        }
+      }
       uint32_t vr[16];
 #pragma unroll
       for (int k = 0; k < 4; ++k)
@@ -306,37 +329,16 @@ __global__ void __launch_bounds__((kW + 1) * 32, (kW <= 4 ? 3 : 2))
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_s + 8 * st);  // stage may be refilled now
       if (kMode == 1) {
-        acc[0][0] += __uint_as_float((kr[0][0].x ^ kr[1][1].w ^ vr[0] ^ vr[15]) & 0x007fffffu);
+        acc[0][0] += __uint_as_float((__float_as_uint(sa[0][0]) ^ vr[0] ^ vr[15]) & 0x007fffffu);
         continue;
-      }
-
-      // ---- S = Q K^T: K bytes become 1024+u exactly (sign flip + exponent bytes);
-      // the (1024 + zp) offset is removed per page with qsum -------------------------
-      float sa[2][2][4];
-#pragma unroll
-      for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int bb = 0; bb < 2; ++bb)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) sa[a][bb][k] = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const uint4 kv = kr[nt][jj >> 2];
-          const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
-          const uint32_t x = w ^ 0x80808080u;
-          mma_16816(sa[nt][jj & 1], qh[2 * jj], 0u, qh[2 * jj + 1], 0u, prmt(x, kMagic, 0x5140u),
-                    prmt(x, kMagic, 0x5342u));
-        }
       }
       const float f = ks * p.qk_scale_log2;
       const float zq = -(1024.0f + (float)kz) * qsum;
       float t[4];
-      t[0] = fmaf(1.f, sa[0][0][0] + sa[0][1][0], zq) * f;  // token 2c
-      t[1] = fmaf(1.f, sa[0][0][1] + sa[0][1][1], zq) * f;  // token 2c+1
-      t[2] = fmaf(1.f, sa[1][0][0] + sa[1][1][0], zq) * f;  // token 8+2c
-      t[3] = fmaf(1.f, sa[1][0][1] + sa[1][1][1], zq) * f;  // token 9+2c
+      t[0] = (sa[0][0] + zq) * f;  // token 2c
+      t[1] = (sa[0][1] + zq) * f;  // token 2c+1
+      t[2] = (sa[1][0] + zq) * f;  // token 8+2c
+      t[3] = (sa[1][1] + zq) * f;  // token 9+2c
       const int pos0 = (p0 + i) * kPage;
       if (pos0 + kPage > len_eff) {
         if (pos0 + 2 * c >= len_eff) t[0] = -INFINITY;
@@ -486,8 +488,97 @@ __global__ void __launch_bounds__((kW + 1) * 32, (kW <= 4 ? 3 : 2))
 // host side
 // ---------------------------------------------------------------------------------
 
-constexpr int kWarpsCfg = 4;    // consumer warps per CTA
-constexpr int kStagesCfg = 16;  // ring stages per CTA
+// CTA shapes (consumer warps, ring stages, CTAs per SM the register budget must allow).
+// FLASHSPEC_NUM_WARPS picks the shape by consumer-warp count (the reference's
+// num_warps knob, triton_utils.py:101-116); FLASHSPEC_KERNEL_SHAPE picks by index.
+struct Shape {
+  int warps, stages, min_blocks;
+};
+using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
+constexpr Shape kShapes[] = {{4, 16, 3}, {4, 8, 4}, {8, 16, 2}};
+constexpr int kNumShapes = 3;
+constexpr int kDefaultShape = 0;
+
+template <bool kPaged, int kSi, int kMode>
+__host__ DecodeKernelFn kernel_inst() {
+  constexpr Shape sh = kShapes[kSi];
+  return decode_kernel<kPaged, sh.warps, sh.stages, sh.min_blocks, kMode>;
+}
+
+template <bool kPaged, int kSi>
+static DecodeKernelFn kernel_mode(int mode) {
+  switch (mode) {
+    case 1: return kernel_inst<kPaged, kSi, 1>();
+    case 2: return kernel_inst<kPaged, kSi, 2>();
+    default: return kernel_inst<kPaged, kSi, 0>();
+  }
+}
+
+template <bool kPaged>
+static DecodeKernelFn kernel_for(int shape, int mode) {
+  switch (shape) {
+    case 1: return kernel_mode<kPaged, 1>(mode);
+    case 2: return kernel_mode<kPaged, 2>(mode);
+    default: return kernel_mode<kPaged, 0>(mode);
+  }
+}
+
+static int smem_bytes(int shape) {
+  const Shape sh = kShapes[shape];
+  return 1024 + sh.stages * (kStageBytes + kMetaBytes + 16);
+}
+
+// FLASHSPEC_DEBUG_MODE (profiling only, results are wrong when set): 1 = skip the math,
+// 2 = data movement only.
+static int debug_mode() {
+  const char* v = getenv("FLASHSPEC_DEBUG_MODE");
+  const int m = v ? atoi(v) : 0;
+  return (m == 1 || m == 2) ? m : 0;
+}
+
+static int shape_choice() {
+  if (const char* v = getenv("FLASHSPEC_KERNEL_SHAPE")) {
+    const int s = atoi(v);
+    if (s >= 0 && s < kNumShapes) return s;
+  }
+  if (const char* v = getenv("FLASHSPEC_NUM_WARPS")) {
+    const int w = atoi(v);
+    for (int s = 0; s < kNumShapes; ++s)
+      if (kShapes[s].warps == w) return s;
+  }
+  return kDefaultShape;
+}
+
+template <bool kPaged>
+static int configure_kernel(int device, int shape) {
+  static bool done[2][kNumShapes][kMaxDevices] = {};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (device < 0 || device >= kMaxDevices) return FS_ERR_CUDA;
+  if (done[kPaged][shape][device]) return FS_OK;
+  for (int mode = 0; mode < 3; ++mode)
+    if (cudaFuncSetAttribute(kernel_for<kPaged>(shape, mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem_bytes(shape)) != cudaSuccess)
+      return FS_ERR_CUDA;
+  done[kPaged][shape][device] = true;
+  return FS_OK;
+}
+
+static int resident_ctas(int device, int shape) {
+  static int cached[kNumShapes][kMaxDevices] = {};
+  static std::mutex mu;
+  // the occupancy query needs the kernel's dynamic shared-memory limit raised first
+  if (configure_kernel<true>(device, shape) != FS_OK) return device_sm_count(device);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[shape][device] > 0) return cached[shape][device];
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for<true>(shape, 0),
+                                                    (kShapes[shape].warps + 1) * 32, smem_bytes(shape)) != cudaSuccess ||
+      per_sm <= 0)
+    per_sm = 1;
+  cached[shape][device] = per_sm * device_sm_count(device);
+  return cached[shape][device];
+}
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -506,7 +597,8 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// View of an int8 KV array as rows of 128 bytes; one box = one 16-row page block.
+// View of an int8 KV array as rows of 128 bytes; one box = one 16-row page block,
+// landing in shared memory with the 128-byte swizzle.
 static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return FS_ERR_CUDA;
@@ -520,58 +612,6 @@ static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
   return r == CUDA_SUCCESS ? FS_OK : FS_ERR_CUDA;
 }
 
-using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
-
-// FLASHSPEC_DEBUG_MODE (profiling only, results are wrong when set): 1 = skip the math,
-// 2 = data movement only.
-static int debug_mode() {
-  const char* v = getenv("FLASHSPEC_DEBUG_MODE");
-  const int m = v ? atoi(v) : 0;
-  return (m == 1 || m == 2) ? m : 0;
-}
-
-template <bool kPaged>
-static DecodeKernelFn kernel_for(int mode) {
-  switch (mode) {
-    case 1: return decode_kernel<kPaged, kWarpsCfg, kStagesCfg, 1>;
-    case 2: return decode_kernel<kPaged, kWarpsCfg, kStagesCfg, 2>;
-    default: return decode_kernel<kPaged, kWarpsCfg, kStagesCfg, 0>;
-  }
-}
-
-template <bool kPaged>
-static int configure_kernel(int device) {
-  static bool done[2][kMaxDevices] = {};
-  static std::mutex mu;
-  std::lock_guard<std::mutex> lock(mu);
-  if (device < 0 || device >= kMaxDevices) return FS_ERR_CUDA;
-  if (done[kPaged][device]) return FS_OK;
-  using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
-  for (int mode = 0; mode < 3; ++mode)
-    if (cudaFuncSetAttribute(kernel_for<kPaged>(mode), cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kTotal) !=
-        cudaSuccess)
-      return FS_ERR_CUDA;
-  done[kPaged][device] = true;
-  return FS_OK;
-}
-
-static int resident_ctas(int device) {
-  static int cached[kMaxDevices] = {};
-  static std::mutex mu;
-  // the occupancy query needs the kernel's dynamic shared-memory limit raised first
-  if (configure_kernel<true>(device) != FS_OK) return device_sm_count(device);
-  std::lock_guard<std::mutex> lock(mu);
-  if (cached[device] > 0) return cached[device];
-  int per_sm = 0;
-  using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for<true>(0),
-                                                    (kWarpsCfg + 1) * 32, Lay::kTotal) != cudaSuccess ||
-      per_sm <= 0)
-    per_sm = 1;
-  cached[device] = per_sm * device_sm_count(device);
-  return cached[device];
-}
-
 static int64_t max_pages_of(const FsDecodeArgs* a) {
   int64_t np = ((int64_t)a->max_seq_len + kPage - 1) / kPage;
   if (a->layout == FS_LAYOUT_PAGED)
@@ -583,13 +623,13 @@ static int64_t max_pages_of(const FsDecodeArgs* a) {
   return hi > lo ? hi - lo : 0;
 }
 
-static int resolve_splits(const FsDecodeArgs* a, int device) {
+static int resolve_splits(const FsDecodeArgs* a, int device, int shape) {
   if (a->num_splits > 0) return a->num_splits;
   const int64_t pairs = (int64_t)a->batch * a->kv_heads;
   const int64_t maxp = max_pages_of(a);
-  const int64_t target = 4LL * resident_ctas(device);
+  const int64_t target = 4LL * resident_ctas(device, shape);
   int64_t s = (target + pairs - 1) / (pairs > 0 ? pairs : 1);
-  const int64_t cap = maxp / (kWarpsCfg * 4);  // at least ~4 pages per warp
+  const int64_t cap = maxp / (kShapes[shape].warps * 4);  // at least ~4 pages per warp
   if (s > cap) s = cap;
   if (s < 1) s = 1;
   if (s > 64) s = 64;
@@ -641,8 +681,9 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   if (st != FS_OK) return st;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
-  if ((st = configure_kernel<kPaged>(device)) != FS_OK) return st;
-  const int splits = resolve_splits(a, device);
+  const int shape = shape_choice();
+  if ((st = configure_kernel<kPaged>(device, shape)) != FS_OK) return st;
+  const int splits = resolve_splits(a, device, shape);
   const size_t need = workspace_for(a, splits);
   if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need)) return FS_ERR_WORKSPACE;
   if (splits > 1 && (a->tickets == nullptr || a->ticket_count < (int64_t)a->batch * a->kv_heads))
@@ -686,10 +727,9 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
     p.part_lse = reinterpret_cast<float*>(ws + align256(units * kD * 4));
     p.counters = reinterpret_cast<unsigned*>(a->tickets);
   }
-  using Lay = SmemLayout<kWarpsCfg, kStagesCfg>;
   const int64_t grid = (int64_t)a->batch * a->kv_heads * splits;
   if (grid >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
-  kernel_for<kPaged>(debug_mode())<<<(unsigned)grid, (kWarpsCfg + 1) * 32, Lay::kTotal,
+  kernel_for<kPaged>(shape, debug_mode())<<<(unsigned)grid, (kShapes[shape].warps + 1) * 32, smem_bytes(shape),
                                      reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
   return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
 }
@@ -704,7 +744,7 @@ int fs_decode_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* spli
   if (st != FS_OK) return st;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
-  const int s = fsb::resolve_splits(a, device);
+  const int s = fsb::resolve_splits(a, device, fsb::shape_choice());
   *bytes = fsb::workspace_for(a, s);
   if (splits_out) *splits_out = s;
   return FS_OK;
