@@ -18,7 +18,7 @@ FS_LAYOUT_CONTIGUOUS, FS_LAYOUT_PAGED = 0, 1
 FS_DEV_BAD_PAGE, FS_DEV_TIMEOUT = 1, 2
 ABI_VERSION = 1
 
-_STATUS_EXC = {1: ValueError, 2: ValueError, 3: RuntimeError, 4: RuntimeError, 5: ValueError}
+_STATUS_EXC = {1: ValueError, 2: ValueError, 3: RuntimeError, 4: RuntimeError, 5: ValueError, 6: ValueError}
 
 
 class FsDecodeArgs(C.Structure):
@@ -118,6 +118,7 @@ SIGNATURES = {
     "fs_decode_workspace_size": (C.c_int, [C.POINTER(FsDecodeArgs), C.POINTER(C.c_size_t), C.POINTER(C.c_int32)]),
     "fs_fused_decode": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
     "fs_paged_decode": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
+    "fs_paged_decode_noalloc": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
     "fs_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_void_p,
                                     C.c_int32, C.c_void_p]),
     "fs_quantize_blocks": (C.c_int, [C.POINTER(FsQuantizeArgs), C.c_void_p]),

@@ -201,6 +201,7 @@ const char* fs_status_string(int s) {
     case FS_ERR_CUDA: return "CUDA error";
     case FS_ERR_WORKSPACE: return "workspace missing or too small";
     case FS_ERR_ALIGNMENT: return "pointer misaligned";
+    case FS_ERR_SCRATCH_LIMIT: return "request exceeds the fixed scratch of fs_paged_decode_noalloc";
     default: return "unknown status";
   }
 }

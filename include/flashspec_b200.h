@@ -33,7 +33,9 @@ typedef enum FsStatus {
   FS_ERR_UNSUPPORTED = 2,      /* valid input outside the kernel's limits    */
   FS_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed          */
   FS_ERR_WORKSPACE = 4,        /* workspace missing or too small             */
-  FS_ERR_ALIGNMENT = 5         /* pointer not aligned as the kernel needs    */
+  FS_ERR_ALIGNMENT = 5,        /* pointer not aligned as the kernel needs    */
+  FS_ERR_SCRATCH_LIMIT = 6     /* request needs more than the fixed scratch of
+                                  fs_paged_decode_noalloc                     */
 } FsStatus;
 
 /* bits OR-ed into the optional device status word by kernels */
@@ -102,6 +104,19 @@ int fs_fused_decode(const FsDecodeArgs* args, void* stream);
  * and _paged_quant_attention_kernel (triton_paged.py:120-299), adding split-K,
  * GQA and page windows.  args->layout must be FS_LAYOUT_PAGED. */
 int fs_paged_decode(const FsDecodeArgs* args, void* stream);
+
+/* Paged decode attention that allocates nothing, for callers that cannot provide
+ * device memory and must not see the library allocate it (e.g. a plugin whose host
+ * owns every device allocation, or a loop that cannot tolerate cudaMalloc's implicit
+ * synchronisation).  No counterpart in the reference: it is fs_paged_decode with the
+ * workspace/tickets fields ignored and replaced by one fixed scratch array compiled
+ * into the library (8 MiB of split partials + 256 KiB of counters, held on every GPU
+ * that loads the library until exit).  Limits: batch*kv_heads <= 65536 and
+ * batch*kv_heads*splits*(q_heads/kv_heads)*516 bytes (rounded) <= 8 MiB, else
+ * FS_ERR_SCRATCH_LIMIT (checked before any launch).  The first call on a device looks
+ * up the array's device address (make it before any stream capture).  All calls share
+ * the array: calls that may overlap on the GPU race and must be serialised. */
+int fs_paged_decode_noalloc(const FsDecodeArgs* args, void* stream);
 
 /* Log-sum-exp merge of n_parts partial results (split-K partials, or per-GPU
  * shards gathered over NVLink).  o_parts fp32 [n_parts, rows, head_dim],
