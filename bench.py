@@ -139,7 +139,7 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_workload(config: str, rank: int):
+def build_workload(config: str, rank: int, world: int = 1):
     from flashspec_b200 import configs
 
     seed = 1000 * rank
@@ -147,7 +147,7 @@ def build_workload(config: str, rank: int):
         return configs.cfg1(seed=seed)
     if config == "cfg2":
         return configs.cfg2(seed=seed)
-    return configs.cfg3(seed=seed)
+    return configs.cfg3_shard(rank, world)
 
 
 # ------------------------------------------------------------------------------------
@@ -257,12 +257,21 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    wl = build_workload(args.config, rank)
+    wl = build_workload(args.config, rank, world)
     q, cache = wl.q, wl.cache
     splits = wl.num_splits
+    seqshard = args.config == "cfg3"
+    if seqshard:
+        from flashspec_b200.dist import SequenceShardedDecoder
 
-    def call():
-        return fs.paged_quant_attention_cuda(q, cache, num_splits=splits)
+        decoder = SequenceShardedDecoder()
+        n_pages = cache.block_table.shape[1]
+
+        def call():
+            return decoder(q, cache, n_pages)
+    else:
+        def call():
+            return fs.paged_quant_attention_cuda(q, cache, num_splits=splits)
 
     def barrier():
         if world > 1:
@@ -316,7 +325,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         q_dev.copy_(q_host, non_blocking=True)
         table_dev.copy_(table_host, non_blocking=True)
         lengths_dev.copy_(lengths_host, non_blocking=True)
-        out = fs.paged_quant_attention_cuda(q_dev, cache_e2e, num_splits=splits)
+        if seqshard:
+            out = decoder(q_dev, cache_e2e, n_pages)
+        else:
+            out = fs.paged_quant_attention_cuda(q_dev, cache_e2e, num_splits=splits)
         out_host.copy_(out, non_blocking=True)
 
     for _ in range(3):
@@ -341,19 +353,24 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         return
 
     peak, peak_kind = measured_peaks()
-    achieved_gbs = wl.bytes_per_call / (launch_ms * 1e-3) / 1e9
-    total_bytes = wl.bytes_per_call * world * args.steps
+    # bytes one rank's decode moves (cfg3: its own page window + q/out + table), per step
+    launch_bytes = wl.bytes_per_call // world if seqshard else wl.bytes_per_call
+    achieved_gbs = launch_bytes / (launch_ms * 1e-3) / 1e9
+    calls_bytes = wl.bytes_per_call * (1 if seqshard else world)  # cfg3: one call spans all ranks
+    total_bytes = calls_bytes * args.steps
     value = total_bytes / (elapsed_ms * 1e-3) / 1e12
-    e2e_value = wl.bytes_per_call * world * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    e2e_value = calls_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
     clocks = sampler.summary(t_soak, t_wall1) if sampler is not None else {}
     line = {
         "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": elapsed_ms / args.steps,
-        "us_per_call": elapsed_ms / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "us_per_call": elapsed_ms / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if seqshard else "weak",
         "vs_baseline": None, "dtype": "int8 KV, fp16 q/out, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": wl.name, "global_batch": len(wl.lengths) * world, "seq_len": max(wl.lengths),
-                   "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "page": 16,
-                   "parallelism": f"request-shard x{world}" if world > 1 else "single",
+        "config": {"workload": wl.name, "global_batch": len(wl.lengths) * (1 if seqshard else world),
+                   "seq_len": max(wl.lengths), "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "page": 16,
+                   "parallelism": (f"sequence-shard x{world} (NCCL all-gather of O/LSE + merge)" if seqshard
+                                   else f"request-shard x{world}" if world > 1 else "single"),
                    "l2": "inputs larger than L2 (no flush)", "bytes_per_call_per_gpu": wl.bytes_per_call},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                      "frac": achieved_gbs / peak, "traffic": traffic_per_launch(args.config),
@@ -362,10 +379,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_call": e2e_ms / e2e_steps * 1e3,
                 "api": "flashspec_b200.paged_quant_attention_cuda with q/table/lengths from pinned host"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (2 if seqshard else 1),
         "clocks": clocks,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and not seqshard:
         n_req = 2 if args.config != "cfg3" else 1
         full_s, ts = time_cpu_baseline(wl, n_req, reps=3)
         line["cpu_baseline"] = {

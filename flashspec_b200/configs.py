@@ -153,3 +153,30 @@ def cfg0(seed: int = 0, device="cuda") -> FusedWorkload:
     del v
     q = torch.randn((b, h, HEAD_DIM), generator=gen, device=device, dtype=torch.float16)
     return FusedWorkload("cfg0_fused_b8_h32_s2048", q, kq, vq, None, algorithmic_bytes(b, h, h, [s] * b))
+
+
+def cfg3_shard(rank: int, world: int, seed: int = 0, device="cuda", seq: int = 131072) -> PagedWorkload:
+    """Config 3 as seen by one rank of a sequence-sharded run: only the logical pages
+    ``page_window(n_pages, rank, world)`` of each of the 2 requests are resident (in a
+    local pool with 10% slack, shuffled); the block_table has the full width with -1
+    outside the window.  q is identical on every rank.  ``bytes_per_call`` is the
+    algorithmic size of the WHOLE call (all ranks together)."""
+    from .dist import page_window
+
+    device = torch.device(device)
+    b, hq, hkv = 2, 64, 8
+    n_pages = (seq + PAGE - 1) // PAGE
+    lo, hi = page_window(n_pages, rank, world)
+    local = (hi - lo) * b
+    pool_pages = max(1, int(math.ceil(local * 1.10)))
+    gen = _gen(seed + 7919 * (rank + 1), device)
+    kq = _quant_pool(pool_pages, hkv, gen, device)
+    vq = _quant_pool(pool_pages, hkv, gen, device)
+    perm = torch.randperm(pool_pages, generator=_gen(seed + 31 * (rank + 1), "cpu"))[:local]
+    table = torch.full((b, n_pages), -1, dtype=torch.int64)
+    table[:, lo:hi] = perm.reshape(b, hi - lo)
+    q = torch.randn((b, hq, HEAD_DIM), generator=_gen(seed, device), device=device, dtype=torch.float16)
+    lens = torch.full((b,), seq, dtype=torch.int64, device=device)
+    cache = PagedKVCache(kq, vq, table.to(device), lens, PAGE, seq)
+    nbytes = algorithmic_bytes(b, hq, hkv, [seq] * b, table_cols=n_pages)
+    return PagedWorkload(f"cfg3_long_b2_64q8kv_s{seq}_seqshard{world}", q, cache, [seq] * b, hq, hkv, None, nbytes)

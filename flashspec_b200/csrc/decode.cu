@@ -456,27 +456,63 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+  // weights of the S partials per query, computed once into shared memory (the ring is
+  // free now): w[s][q] = exp(lse_s - M) / sum_s exp(lse_s - M); empty partials weigh 0
+  float* wsm = reinterpret_cast<float*>(base_p);  // [S][G] (+ [G] merged LSE)
+  const int nw = S * p.G;
+  const bool fits = (nw + p.G) * 4 <= L::kStageRegion;
+  if (fits) {
+    const size_t prow0 = (size_t)bh * S * p.G;
+    for (int k = tid; k < nw; k += kThreads) wsm[k] = __ldcg(p.part_lse + prow0 + k);
+    __syncthreads();
+    if (tid < p.G) {
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, wsm[s2 * p.G + tid]);
+      float W = 0.f;
+      if (M != -INFINITY)
+        for (int s2 = 0; s2 < S; ++s2) {
+          const float l = wsm[s2 * p.G + tid];
+          const float w = l == -INFINITY ? 0.f : expf(l - M);
+          wsm[s2 * p.G + tid] = w;
+          W += w;
+        }
+      const float inv = W > 0.f ? 1.f / W : 0.f;
+      for (int s2 = 0; s2 < S; ++s2) wsm[s2 * p.G + tid] = M == -INFINITY ? 0.f : wsm[s2 * p.G + tid] * inv;
+      wsm[nw + tid] = W > 0.f ? M + logf(W) : -INFINITY;
+    }
+    __syncthreads();
+  }
   for (int idx = tid; idx < nout; idx += kThreads) {
     const int qg = idx >> 7;
     const int d = idx & (kD - 1);
     const size_t prow0 = (size_t)bh * S * p.G + qg;
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(p.part_lse + prow0 + (size_t)s2 * p.G));
-    float W = 0.f, O = 0.f;
-    if (M != -INFINITY) {
+    float o = 0.f, lse_out;
+    if (fits) {
       for (int s2 = 0; s2 < S; ++s2) {
-        const size_t pr = prow0 + (size_t)s2 * p.G;
-        const float lse = __ldcg(p.part_lse + pr);
-        const float w = lse == -INFINITY ? 0.f : expf(lse - M);
-        W += w;
-        O += w * __ldcg(p.part_o + pr * kD + d);
+        const float w = wsm[s2 * p.G + qg];
+        if (w != 0.f) o = fmaf(w, __ldcg(p.part_o + (prow0 + (size_t)s2 * p.G) * kD + d), o);
       }
+      lse_out = wsm[nw + qg];
+    } else {
+      float M = -INFINITY;
+      for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(p.part_lse + prow0 + (size_t)s2 * p.G));
+      float W = 0.f, O = 0.f;
+      if (M != -INFINITY) {
+        for (int s2 = 0; s2 < S; ++s2) {
+          const size_t pr = prow0 + (size_t)s2 * p.G;
+          const float lse = __ldcg(p.part_lse + pr);
+          const float w = lse == -INFINITY ? 0.f : expf(lse - M);
+          W += w;
+          O += w * __ldcg(p.part_o + pr * kD + d);
+        }
+      }
+      o = W > 0.f ? O / W : 0.f;
+      lse_out = W > 0.f ? M + logf(W) : -INFINITY;
     }
-    const float o = W > 0.f ? O / W : 0.f;
     const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
     if (p.shard_o != nullptr) {
       p.shard_o[row * kD + d] = o;
-      if (d == 0) p.shard_lse[row] = W > 0.f ? M + logf(W) : -INFINITY;
+      if (d == 0) p.shard_lse[row] = lse_out;
     } else {
       p.out[row * kD + d] = __float2half_rn(o);
     }
@@ -623,17 +659,38 @@ static int64_t max_pages_of(const FsDecodeArgs* a) {
   return hi > lo ? hi - lo : 0;
 }
 
+// Split policy.  Every CTA carries a fixed cost (set-up latency before its first page
+// lands, the warp merge, the ticket) worth roughly kCtaOverheadPages pages of streaming,
+// and CTAs run in waves of `slots` (resident CTAs).  With fewer (request, kv head) pairs
+// than slots, split to fill exactly one wave; otherwise pick the S minimising
+// waves(S) * (pages per CTA + overhead).  Fitted on B200 sweeps of the benchmark
+// configurations.
 static int resolve_splits(const FsDecodeArgs* a, int device, int shape) {
   if (a->num_splits > 0) return a->num_splits;
+  constexpr int64_t kCtaOverheadPages = 24;
   const int64_t pairs = (int64_t)a->batch * a->kv_heads;
   const int64_t maxp = max_pages_of(a);
-  const int64_t target = 4LL * resident_ctas(device, shape);
-  int64_t s = (target + pairs - 1) / (pairs > 0 ? pairs : 1);
-  const int64_t cap = maxp / (kShapes[shape].warps * 4);  // at least ~4 pages per warp
-  if (s > cap) s = cap;
-  if (s < 1) s = 1;
-  if (s > 64) s = 64;
-  return (int)s;
+  const int64_t slots = resident_ctas(device, shape);
+  const int64_t cap = maxp / (kShapes[shape].warps * 4) > 1 ? maxp / (kShapes[shape].warps * 4) : 1;
+  if (pairs <= 0 || maxp <= 0) return 1;
+  int64_t best = 1;
+  if (pairs <= slots / 2) {
+    best = slots / pairs;
+  } else {
+    double best_cost = 1e300;
+    for (int64_t s = 1; s <= 64; ++s) {
+      const int64_t waves = (pairs * s + slots - 1) / slots;
+      const double cost = (double)waves * (double)((maxp + s - 1) / s + kCtaOverheadPages);
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = s;
+      }
+    }
+  }
+  if (best > cap) best = cap;
+  if (best < 1) best = 1;
+  if (best > 256) best = 256;
+  return (int)best;
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
