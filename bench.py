@@ -47,7 +47,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg1", "cfg2", "cfg3"], default="cfg1")
+    ap.add_argument("--config", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1.5 s clock soak (for profiler launch lists)")
     return ap.parse_args()
@@ -393,13 +393,50 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     print(json.dumps(line), flush=True)
 
 
+def run_serving(args, rank: int, world: int, local_rank: int):
+    """cfg4: the allocator-driven serving loop; a step is one decode step of the loop
+    (admission/prefill, append of one token per live request, attention, release)."""
+    import torch
+
+    from flashspec_b200.serving import ServingConfig, run
+
+    torch.cuda.set_device(local_rank)
+    cfg = ServingConfig(steps=args.steps, seed=1000 * rank)
+    res = run(cfg, device=f"cuda:{local_rank}")
+    if rank != 0:
+        return
+    step_s = res["step_ms_mean"] * 1e-3
+    moved = res["attention_bytes"] + res["append_bytes"]
+    peak, peak_kind = measured_peaks()
+    att_gbs = res["attention_bytes"] / (res["attention_ms_total"] * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": moved / (sum([res["step_ms_mean"]] * args.steps) * 1e-3) / 1e12 * world,
+        "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": 0, "ms_per_step": res["step_ms_mean"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 KV, fp16 q/out/tokens, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "cfg4_serving_loop", "parallelism": f"request-shard x{world}" if world > 1 else "single",
+                   **{k: v for k, v in cfg.__dict__.items()}},
+        "roofline": {"bound": "hbm", "achieved": att_gbs, "peak": peak, "unit": "GB/s", "frac": att_gbs / peak,
+                     "traffic": None, "peak_kind": f"{peak_kind} copy bandwidth", "kernel": "attention launches"},
+        "serving": res,
+        "gpu_launches": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
+        if args.config == "cfg4":
+            print(json.dumps({"impl": "reference", "unavailable": "cfg4 reference arm not implemented"}))
+            return
         run_reference(args, rank, world)
+        return
+    if args.config == "cfg4":
+        run_serving(args, rank, world, local_rank)
         return
     if world > 1:
         import torch
