@@ -96,10 +96,249 @@ struct SmemLayout {
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent bytes: half 0x64xx == 1024 + xx
 
-// One CTA = one (request, kv head, split).  Warps 0..kW-1 consume pages; warp kW is the
-// producer that keeps the ring full with TMA tile loads and cp.async qparam copies.
-// kMode is a profiling aid: 0 = normal; 1 = consumers read the stage and release it but
-// skip the math; 2 = consumers only wait and release (pure data movement).
+// qparams of one stage as the consumers read them
+struct StageInfo {
+  float ks, vs;
+  uint32_t kz, vz;
+};
+
+// Producer side, one lane: fill stage `st` with the (page, kv head) block whose index in
+// the [blocks, 16, 128] view is `e` (< 0: nothing to load, the stage is marked invalid).
+__device__ __forceinline__ void issue_page(const DecodeParams& p, const CUtensorMap* tmk, const CUtensorMap* tmv,
+                                           uint32_t base_s, uint32_t* meta_p, uint32_t meta_s, uint32_t full,
+                                           int st, int64_t e, uint64_t policy) {
+  uint32_t* m = meta_p + st * (kMetaBytes / 4);
+  if (e < 0) {
+    m[4] = 0u;
+    mbar_arrive(full);
+    mbar_arrive(full);
+    return;
+  }
+  const bool word_ok = (e | 1) < p.zp_count;
+  if (!word_ok) {  // last element of an odd-sized zero-point array: plain loads
+    m[2] = (uint32_t)(uint16_t)p.k_zero[e];
+    m[3] = (uint32_t)(uint16_t)p.v_zero[e];
+  }
+  m[4] = 1u | (word_ok ? ((uint32_t)(e & 1) << 1) : 0u);
+  mbar_arrive_expect_tx(full, kStageBytes);
+  const uint32_t dst = base_s + st * kStageBytes;
+  tma_load_2d(dst, tmk, 0, (int32_t)(e * kPage), full, policy);
+  tma_load_2d(dst + kPageBytes, tmv, 0, (int32_t)(e * kPage), full, policy);
+  const uint32_t ms = meta_s + st * kMetaBytes;
+  cp_async_4(ms + 0, p.k_scale + e);
+  cp_async_4(ms + 4, p.v_scale + e);
+  if (word_ok) {
+    cp_async_4(ms + 8, p.k_zero + (e & ~1ll));
+    cp_async_4(ms + 12, p.v_zero + (e & ~1ll));
+  }
+  cp_async_mbar_arrive_noinc(full);
+}
+
+// Index of the (page, kv head) block of table entry `phys` (paged) or logical page `phys`
+// (contiguous); -1 when the entry is unallocated or outside the pool (the latter is
+// reported in the status word).
+template <bool kPaged>
+__device__ __forceinline__ int64_t block_index(const DecodeParams& p, int b, int h, long long phys) {
+  if (kPaged) {
+    if (phys < 0) return -1;
+    if (phys >= p.num_blocks) {
+      if (p.status != nullptr) atomicOr(p.status, FS_DEV_BAD_PAGE);
+      return -1;
+    }
+    return (int64_t)phys * p.Hkv + h;
+  }
+  return ((int64_t)b * p.Hkv + h) * p.num_blocks + phys;
+}
+
+__device__ __forceinline__ bool read_stage_info(const uint32_t* meta_p, int st, StageInfo& si) {
+  const volatile uint32_t* m = meta_p + st * (kMetaBytes / 4);
+  const uint32_t flags = m[4];
+  if (!(flags & 1u)) return false;
+  si.ks = __uint_as_float(m[0]);
+  si.vs = __uint_as_float(m[1]);
+  const uint32_t sh = (flags & 2u) ? 16u : 0u;
+  si.kz = (m[2] >> sh) & 0xffffu;
+  si.vz = (m[3] >> sh) & 0xffffu;
+  return true;
+}
+
+// Per-thread shared-memory offsets inside a stage (128-byte swizzle: the 16-byte chunk
+// index of row r is XOR-ed with r & 7).  K: rows g and g+8, chunks 2c and 2c+1.  V:
+// ldmatrix.x4.trans #k reads 8x8 b16 matrices (chunk 2k | 2k+1) x (tokens 0-7 | 8-15);
+// lane l supplies row (l & 7) of matrix (l >> 3).
+struct StageOffsets {
+  uint32_t k[2][2];
+  uint32_t v[4];
+  __device__ __forceinline__ explicit StageOffsets(int lane) {
+    const int g = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) k[nt][e2] = (g + 8 * nt) * 128 + (((2 * c + e2) ^ g) << 4);
+    const int mat = lane >> 3, r = lane & 7;
+    const int tok = 8 * (mat & 1) + r;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) v[kk] = kPageBytes + tok * 128 + (((2 * kk + (mat >> 1)) ^ r) << 4);
+  }
+};
+
+// Query fragment of one (request, kv head): thread (g,c) holds q[g][32c .. 32c+32) as the A
+// operand of S = Q K^T (logical k 2c,2c+1 | 2c+8,2c+9 of step j = head dim 32c+4j+0,1 | 2,3)
+// and qsum = the sum of the same fp16 values of row g.
+struct QueryFrag {
+  uint32_t qh[16];
+  float qsum;
+  __device__ __forceinline__ void load(const DecodeParams& p, int b, int h, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    qsum = 0.f;
+    if (g < p.G) {
+      const uint4* qp =
+          reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.Hq + (size_t)h * p.G + g) * kD + 32 * c);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = __ldg(qp + i);
+        qh[4 * i + 0] = v.x;
+        qh[4 * i + 1] = v.y;
+        qh[4 * i + 2] = v.z;
+        qh[4 * i + 3] = v.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&qh[i]));
+        qsum += f2.x + f2.y;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qh[i] = 0u;
+    }
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+  }
+};
+
+// Online-softmax state of one warp: running max (log2 domain, finite so exp2 never sees
+// inf - inf), this thread's share of the denominator, and the PV accumulator
+// acc[i][0..3] = O[d = 16i+2g (+1 for [2],[3])][query 2c | 2c+1].
+struct WarpState {
+  float m_run, l_run;
+  float acc[8][4];
+  __device__ __forceinline__ void reset() {
+    m_run = -1.0e30f;
+    l_run = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[i][k] = 0.f;
+  }
+};
+
+// Consumer side: load stage `sbase`, release it on `empty_bar`, then fold the page into
+// the warp state.  pos0 = first token position of the page, len_eff = tokens that count.
+// kMode 1 stops after the loads (profiling).
+template <int kMode>
+__device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets& off, uint32_t empty_bar, int lane,
+                                             const StageInfo& si, const QueryFrag& qf, float qk_scale_log2,
+                                             int pos0, int len_eff, WarpState& ws) {
+  const int c = lane & 3;
+  // ---- S = Q K^T: K bytes become 1024+u exactly (sign flip + exponent bytes); the
+  // (1024 + zp) offset is removed per page with qsum -------------------------------
+  float sa[2][4];
+  {
+    uint4 kr[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sbase + off.k[nt][e2]);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sa[nt][k] = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint4 kv = kr[nt][jj >> 2];
+        const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
+        const uint32_t x = w ^ 0x80808080u;
+        mma_16816(sa[nt], qf.qh[2 * jj], 0u, qf.qh[2 * jj + 1], 0u, prmt(x, kMagic, 0x5140u),
+                  prmt(x, kMagic, 0x5342u));
+      }
+    }
+  }
+  uint32_t vr[16];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) ldsm_x4_trans(sbase + off.v[k], vr[4 * k], vr[4 * k + 1], vr[4 * k + 2], vr[4 * k + 3]);
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled now
+  if (kMode == 1) {
+    ws.acc[0][0] += __uint_as_float((__float_as_uint(sa[0][0]) ^ vr[0] ^ vr[15]) & 0x007fffffu);
+    return;
+  }
+  const float f = si.ks * qk_scale_log2;
+  const float zq = -(1024.0f + (float)si.kz) * qf.qsum;
+  float t[4];
+  t[0] = (sa[0][0] + zq) * f;  // token 2c
+  t[1] = (sa[0][1] + zq) * f;  // token 2c+1
+  t[2] = (sa[1][0] + zq) * f;  // token 8+2c
+  t[3] = (sa[1][1] + zq) * f;  // token 9+2c
+  if (pos0 + kPage > len_eff) {
+    if (pos0 + 2 * c >= len_eff) t[0] = -INFINITY;
+    if (pos0 + 2 * c + 1 >= len_eff) t[1] = -INFINITY;
+    if (pos0 + 8 + 2 * c >= len_eff) t[2] = -INFINITY;
+    if (pos0 + 9 + 2 * c >= len_eff) t[3] = -INFINITY;
+  }
+  float mx = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  if (__any_sync(0xffffffffu, mx > ws.m_run)) {
+    const float m_new = fmaxf(ws.m_run, mx);
+    const float alpha = ex2_approx(ws.m_run - m_new);
+    ws.m_run = m_new;
+    ws.l_run *= alpha;
+    const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
+    const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+#pragma unroll
+    for (int i2 = 0; i2 < 8; ++i2) {
+      ws.acc[i2][0] *= a0;
+      ws.acc[i2][1] *= a1;
+      ws.acc[i2][2] *= a0;
+      ws.acc[i2][3] *= a1;
+    }
+  }
+  float pr[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) pr[k] = ex2_approx(t[k] - ws.m_run);
+  ws.l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
+  const uint32_t pb0 = pack_half2(pr[0] * si.vs, pr[1] * si.vs);
+  const uint32_t pb1 = pack_half2(pr[2] * si.vs, pr[3] * si.vs);
+  // ---- O += P V: vr(chunk i, tokens 0-7 | 8-15) hold bytes
+  // [V[2c][d], V[2c][d+1], V[2c+1][d], V[2c+1][d+1]] with d = 16i + 2g ---------------
+  const uint32_t zv2 = (0x6400u + si.vz) * 0x10001u;
+#pragma unroll
+  for (int i2 = 0; i2 < 8; ++i2) {
+    const uint32_t x0 = vr[4 * (i2 >> 1) + 2 * (i2 & 1)] ^ 0x80808080u;
+    const uint32_t x1 = vr[4 * (i2 >> 1) + 2 * (i2 & 1) + 1] ^ 0x80808080u;
+    mma_16816(ws.acc[i2], hsub2_u32(prmt(x0, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x0, kMagic, 0x5341u), zv2),
+              hsub2_u32(prmt(x1, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x1, kMagic, 0x5341u), zv2), pb0, pb1);
+  }
+}
+
+// Writes one normalised output value: fp16 `out`, or (O, LSE) into the shard outputs.
+__device__ __forceinline__ void write_final(const DecodeParams& p, size_t row, int d, float o, float lse) {
+  if (p.shard_o != nullptr) {
+    p.shard_o[row * kD + d] = o;
+    if (d == 0) p.shard_lse[row] = lse;
+  } else {
+    p.out[row * kD + d] = __float2half_rn(o);
+  }
+}
+
+// ==================================================================================
+// Split kernel: one CTA = one (request, kv head, split).  Warps 0..kW-1 consume pages;
+// warp kW is the producer that keeps the ring full with TMA tile loads and cp.async
+// qparam copies.  kMode is a profiling aid: 0 = normal; 1 = consumers read the stage and
+// release it but skip the math; 2 = consumers only wait and release (data movement).
+// ==================================================================================
 template <bool kPaged, int kW, int kNS, int kMinBlocks, int kMode>
 __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -150,13 +389,8 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   __syncthreads();
 
   bool aborted = false;
-  float acc[8][4];
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[i][k] = 0.f;
-  float m_run = -1.0e30f;  // running max (log2 domain); finite so exp2 never sees inf-inf
-  float l_run = 0.f;       // this thread's share of the softmax denominator
+  WarpState ws;
+  ws.reset();
 
   if (warp == kW) {
     // ============================ producer warp ===============================
@@ -170,7 +404,6 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     const int64_t* trow = kPaged ? p.table + (size_t)b * p.cols + p0 : nullptr;
     long long tcur = (kPaged && lane < n) ? (long long)trow[lane] : -1;
     long long tnxt = (kPaged && 32 + lane < n) ? (long long)trow[32 + lane] : -1;
-    const int64_t ebase = kPaged ? (int64_t)h : ((int64_t)b * p.Hkv + h) * p.num_blocks;
     for (int i0 = 0; i0 < n; i0 += kIssue) {
       long long phys;
       if (kPaged) {
@@ -185,41 +418,13 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       const int i = i0 + lane;
       if (lane < kIssue && i < n) {
         const int st = i & (kNS - 1);
-        const uint32_t full = full_s + 8 * st;
         if (i >= kNS && !mbar_wait_bounded(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kTimeoutNs)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
-        if (!aborted) {
-          uint32_t* m = meta_p + st * (kMetaBytes / 4);
-          const bool ok = !kPaged || (phys >= 0 && phys < p.num_blocks);
-          if (!ok) {
-            if (phys >= p.num_blocks && p.status != nullptr) atomicOr(p.status, FS_DEV_BAD_PAGE);
-            m[4] = 0u;
-            mbar_arrive(full);
-            mbar_arrive(full);
-          } else {
-            const int64_t e = kPaged ? phys * p.Hkv + ebase : ebase + phys;
-            const bool word_ok = (e | 1) < p.zp_count;
-            if (!word_ok) {  // last element of an odd-sized zero-point array: plain loads
-              m[2] = (uint32_t)(uint16_t)p.k_zero[e];
-              m[3] = (uint32_t)(uint16_t)p.v_zero[e];
-            }
-            m[4] = 1u | (word_ok ? ((uint32_t)(e & 1) << 1) : 0u);
-            mbar_arrive_expect_tx(full, kStageBytes);
-            const uint32_t dst = base_s + st * kStageBytes;
-            tma_load_2d(dst, &tmk, 0, (int32_t)(e * kPage), full, policy);
-            tma_load_2d(dst + kPageBytes, &tmv, 0, (int32_t)(e * kPage), full, policy);
-            const uint32_t ms = meta_s + st * kMetaBytes;
-            cp_async_4(ms + 0, p.k_scale + e);
-            cp_async_4(ms + 4, p.v_scale + e);
-            if (word_ok) {
-              cp_async_4(ms + 8, p.k_zero + (e & ~1ll));
-              cp_async_4(ms + 12, p.v_zero + (e & ~1ll));
-            }
-            cp_async_mbar_arrive_noinc(full);
-          }
-        }
+        if (!aborted)
+          issue_page(p, &tmk, &tmv, base_s, meta_p, meta_s, full_s + 8 * st, st, block_index<kPaged>(p, b, h, phys),
+                     policy);
       }
       if (__any_sync(0xffffffffu, aborted)) {
         aborted = true;
@@ -228,51 +433,9 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     }
   } else {
     // ============================ consumer warps ===============================
-    // query fragment: thread (g,c) holds q[g][32c .. 32c+32) as the A operand of
-    // S = Q K^T, where logical k (2c, 2c+1 | 2c+8, 2c+9) of step j is head dim
-    // 32c+4j+(0,1 | 2,3).  qsum = sum of the same fp16 values (row g).
-    uint32_t qh[16];
-    float qsum = 0.f;
-    if (g < p.G) {
-      const uint4* qp =
-          reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.Hq + (size_t)h * p.G + g) * kD + 32 * c);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = __ldg(qp + i);
-        qh[4 * i + 0] = v.x;
-        qh[4 * i + 1] = v.y;
-        qh[4 * i + 2] = v.z;
-        qh[4 * i + 3] = v.w;
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&qh[i]));
-        qsum += f2.x + f2.y;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) qh[i] = 0u;
-    }
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
-
-    // per-thread offsets inside a stage (128-byte swizzle: the 16-byte chunk index of
-    // row r is XOR-ed with r & 7).  K: rows g and g+8, chunks 2c and 2c+1.
-    uint32_t koff[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e2 = 0; e2 < 2; ++e2) koff[nt][e2] = (g + 8 * nt) * 128 + (((2 * c + e2) ^ g) << 4);
-    // V: ldmatrix.x4.trans #k reads 8x8 b16 matrices (chunk 2k | 2k+1) x (tokens 0-7 | 8-15);
-    // lane l supplies row (l & 7) of matrix (l >> 3).
-    uint32_t voff[4];
-    {
-      const int mat = lane >> 3, r = lane & 7;
-      const int tok = 8 * (mat & 1) + r;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) voff[k] = kPageBytes + tok * 128 + (((2 * k + (mat >> 1)) ^ r) << 4);
-    }
-
+    QueryFrag qf;
+    qf.load(p, b, h, lane);
+    const StageOffsets off(lane);
     for (int i = warp; i < n; i += kW) {
       const int st = i & (kNS - 1);
       if (!mbar_wait_bounded(full_s + 8 * st, (uint32_t)((i / kNS) & 1), kTimeoutNs)) {
@@ -280,110 +443,17 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
         aborted = true;
         break;
       }
-      const volatile uint32_t* m = meta_p + st * (kMetaBytes / 4);
-      const uint32_t flags = m[4];
-      if (!(flags & 1u)) {  // unallocated / rejected page: masked like the reference
+      StageInfo si;
+      if (kMode == 2 || !read_stage_info(meta_p, st, si)) {  // masked page (or data-only profiling)
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_s + 8 * st);
         continue;
       }
-      const float ks = __uint_as_float(m[0]);
-      const float vs = __uint_as_float(m[1]);
-      const uint32_t sh = (flags & 2u) ? 16u : 0u;
-      const uint32_t kz = (m[2] >> sh) & 0xffffu;
-      const uint32_t vz = (m[3] >> sh) & 0xffffu;
-      if (kMode == 2) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_s + 8 * st);
-        continue;
-      }
-      const uint32_t sbase = base_s + st * kStageBytes;
-      // ---- S = Q K^T: K bytes become 1024+u exactly (sign flip + exponent bytes);
-      // the (1024 + zp) offset is removed per page with qsum -------------------------
-      float sa[2][4];
-      {
-        uint4 kr[2][2];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int e2 = 0; e2 < 2; ++e2) kr[nt][e2] = lds128(sbase + koff[nt][e2]);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) sa[nt][k] = 0.f;
-#pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const uint4 kv = kr[nt][jj >> 2];
-            const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
-            const uint32_t x = w ^ 0x80808080u;
-            mma_16816(sa[nt], qh[2 * jj], 0u, qh[2 * jj + 1], 0u, prmt(x, kMagic, 0x5140u), prmt(x, kMagic, 0x5342u));
-          }
-        }
-      }
-      uint32_t vr[16];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        ldsm_x4_trans(sbase + voff[k], vr[4 * k], vr[4 * k + 1], vr[4 * k + 2], vr[4 * k + 3]);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_s + 8 * st);  // stage may be refilled now
-      if (kMode == 1) {
-        acc[0][0] += __uint_as_float((__float_as_uint(sa[0][0]) ^ vr[0] ^ vr[15]) & 0x007fffffu);
-        continue;
-      }
-      const float f = ks * p.qk_scale_log2;
-      const float zq = -(1024.0f + (float)kz) * qsum;
-      float t[4];
-      t[0] = (sa[0][0] + zq) * f;  // token 2c
-      t[1] = (sa[0][1] + zq) * f;  // token 2c+1
-      t[2] = (sa[1][0] + zq) * f;  // token 8+2c
-      t[3] = (sa[1][1] + zq) * f;  // token 9+2c
-      const int pos0 = (p0 + i) * kPage;
-      if (pos0 + kPage > len_eff) {
-        if (pos0 + 2 * c >= len_eff) t[0] = -INFINITY;
-        if (pos0 + 2 * c + 1 >= len_eff) t[1] = -INFINITY;
-        if (pos0 + 8 + 2 * c >= len_eff) t[2] = -INFINITY;
-        if (pos0 + 9 + 2 * c >= len_eff) t[3] = -INFINITY;
-      }
-      float mx = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      if (__any_sync(0xffffffffu, mx > m_run)) {
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = ex2_approx(m_run - m_new);
-        m_run = m_new;
-        l_run *= alpha;
-        const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
-        const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
-#pragma unroll
-        for (int i2 = 0; i2 < 8; ++i2) {
-          acc[i2][0] *= a0;
-          acc[i2][1] *= a1;
-          acc[i2][2] *= a0;
-          acc[i2][3] *= a1;
-        }
-      }
-      float pr[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) pr[k] = ex2_approx(t[k] - m_run);
-      l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
-      const uint32_t pb0 = pack_half2(pr[0] * vs, pr[1] * vs);
-      const uint32_t pb1 = pack_half2(pr[2] * vs, pr[3] * vs);
-
-      // ---- O += P V: vr(chunk i, tokens 0-7 | 8-15) hold bytes
-      // [V[2c][d], V[2c][d+1], V[2c+1][d], V[2c+1][d+1]] with d = 16i + 2g ------------
-      const uint32_t zv2 = (0x6400u + vz) * 0x10001u;
-#pragma unroll
-      for (int i2 = 0; i2 < 8; ++i2) {
-        const uint32_t x0 = vr[4 * (i2 >> 1) + 2 * (i2 & 1)] ^ 0x80808080u;
-        const uint32_t x1 = vr[4 * (i2 >> 1) + 2 * (i2 & 1) + 1] ^ 0x80808080u;
-        mma_16816(acc[i2], hsub2_u32(prmt(x0, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x0, kMagic, 0x5341u), zv2),
-                  hsub2_u32(prmt(x1, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x1, kMagic, 0x5341u), zv2), pb0, pb1);
-      }
+      consume_page<kMode>(base_s + st * kStageBytes, off, empty_s + 8 * st, lane, si, qf, p.qk_scale_log2,
+                          (p0 + i) * kPage, len_eff, ws);
     }
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    ws.l_run += __shfl_xor_sync(0xffffffffu, ws.l_run, 1);
+    ws.l_run += __shfl_xor_sync(0xffffffffu, ws.l_run, 2);
   }
 
   // ---- merge the consumer warps through shared memory ---------------------------
@@ -395,18 +465,18 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   float* accs = ls + kW * kMaxG;  // [kW][kMaxG][kD]
   if (warp < kW) {
     if (c == 0) {
-      ms[warp * kMaxG + g] = m_run;
-      ls[warp * kMaxG + g] = l_run;
+      ms[warp * kMaxG + g] = ws.m_run;
+      ls[warp * kMaxG + g] = ws.l_run;
     }
 #pragma unroll
     for (int i2 = 0; i2 < 8; ++i2) {
       const int d = 16 * i2 + 2 * g;
       float* a0p = accs + (warp * kMaxG + 2 * c) * kD;
       float* a1p = accs + (warp * kMaxG + 2 * c + 1) * kD;
-      a0p[d] = acc[i2][0];
-      a1p[d] = acc[i2][1];
-      a0p[d + 1] = acc[i2][2];
-      a1p[d + 1] = acc[i2][3];
+      a0p[d] = ws.acc[i2][0];
+      a1p[d] = ws.acc[i2][1];
+      a0p[d + 1] = ws.acc[i2][2];
+      a1p[d + 1] = ws.acc[i2][3];
     }
   }
   __syncthreads();
@@ -431,12 +501,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     const float lse = Lsum > 0.f ? (M + log2f(Lsum)) * kLn2 : -INFINITY;
     const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
     if (S == 1) {
-      if (p.shard_o != nullptr) {
-        p.shard_o[row * kD + d] = o;
-        if (d == 0) p.shard_lse[row] = lse;
-      } else {
-        p.out[row * kD + d] = __float2half_rn(o);
-      }
+      write_final(p, row, d, o, lse);
     } else {
       const size_t prow = ((size_t)bh * S + split) * p.G + qg;
       p.part_o[prow * kD + d] = o;
@@ -509,13 +574,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       o = W > 0.f ? O / W : 0.f;
       lse_out = W > 0.f ? M + logf(W) : -INFINITY;
     }
-    const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
-    if (p.shard_o != nullptr) {
-      p.shard_o[row * kD + d] = o;
-      if (d == 0) p.shard_lse[row] = lse_out;
-    } else {
-      p.out[row * kD + d] = __float2half_rn(o);
-    }
+    write_final(p, (size_t)b * p.Hq + (size_t)h * p.G + qg, d, o, lse_out);
   }
   if (tid == 0) p.counters[bh] = 0u;  // leave the ticket clean for the next call
 }
