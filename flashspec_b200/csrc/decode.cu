@@ -35,6 +35,8 @@
 
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
+#include <algorithm>
 #include <mutex>
 #include <stdint.h>
 
@@ -579,6 +581,303 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   if (tid == 0) p.counters[bh] = 0u;  // leave the ticket clean for the next call
 }
 
+// ==================================================================================
+// Balanced kernel (stream-K over pages): a persistent grid of C CTAs with kW consumer
+// warps each.  The flattened work space is every (request, kv head, page of the window)
+// in request-major order, T pages in total; consumer warp k of the Wt = C*kW warps owns
+// the contiguous share [k*T/Wt, (k+1)*T/Wt), so every warp streams the same number of
+// pages whatever the lengths.  Per-request page counts come from `lengths` on the device
+// (a block-wide prefix sum at start), so the host never synchronises.  The producer warp
+// interleaves its CTA's kW shares through one ring (issue index i -> warp i % kW, step
+// i / kW, stage i % kNS).  A consumer warp closes a "piece" whenever its share crosses a
+// (request, kv head) boundary: a piece covering the whole pair writes the output
+// directly; otherwise its normalised (O, LSE) goes to slot 0 (the warp's first piece)
+// or slot 1 (a later piece) and an atomic ticket elects the last contributor of the
+// pair to merge them.
+// ==================================================================================
+constexpr int kMaxSKBatch = 1536;  // requests whose prefix sums fit the shared-memory table
+
+__device__ __forceinline__ int64_t share_start(int64_t k, int64_t T, int64_t Wt) { return k * T / Wt; }
+// warp whose share contains flat page f
+__device__ __forceinline__ int64_t share_of(int64_t f, int64_t T, int64_t Wt) { return ((f + 1) * Wt - 1) / T; }
+
+// largest r with pre[r] <= f (pre ascending, pre[0] = 0, pre[B] = T > f)
+__device__ __forceinline__ int find_request(const int* pre, int B, int f) {
+  int lo = 0, hi = B;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (pre[mid] <= f) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+template <bool kPaged>
+__device__ __forceinline__ int window_pages(const DecodeParams& p, int r, int lo, int hi_cap, int* len_eff) {
+  int64_t len = p.max_seq_len;
+  if (p.lengths != nullptr) len = min(len, p.lengths[r]);
+  len = max(len, (int64_t)0);
+  const int np = kPaged ? min((int)((len + kPage - 1) / kPage), p.cols) : (int)min((len + kPage - 1) / kPage, p.num_blocks);
+  if (len_eff) *len_eff = (int)min(len, (int64_t)np * kPage);
+  return max(0, min(np, hi_cap) - lo);
+}
+
+template <bool kPaged, int kW, int kNS, int kMinBlocks>
+__global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
+    decode_balanced_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                           const DecodeParams p) {
+  using L = SmemLayout<kW, kNS>;
+  constexpr int kThreads = (kW + 1) * 32;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_u32(smem_raw);
+  const uint32_t base_s = (raw_s + 1023u) & ~1023u;
+  uint8_t* base_p = smem_raw + (base_s - raw_s);
+  const uint32_t meta_s = base_s + L::kStageRegion;
+  uint32_t* meta_p = reinterpret_cast<uint32_t*>(base_p + L::kStageRegion);
+  const uint32_t full_s = base_s + L::kStageRegion + L::kMetaRegion;
+  const uint32_t empty_s = full_s + kNS * 8;
+  int* pre = reinterpret_cast<int*>(base_p + L::kStageRegion + L::kMetaRegion + L::kBarRegion);  // [B + 1]
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = p.B, Hkv = p.Hkv;
+  const int lo = (int)max(p.page_begin, (int64_t)0);
+  const int hi_cap = p.page_end > 0 ? (int)min(p.page_end, (int64_t)0x7fffffff) : 0x7fffffff;
+
+  if (tid == 0) {
+    for (int st = 0; st < kNS; ++st) {
+      mbar_init(full_s + 8 * st, 2);
+      mbar_init(empty_s + 8 * st, 1);
+    }
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  for (int r = tid; r < B; r += kThreads) pre[r + 1] = window_pages<kPaged>(p, r, lo, hi_cap, nullptr) * Hkv;
+  __syncthreads();
+  if (warp == 0) {  // inclusive prefix sum of the per-request page counts (x Hkv)
+    int carry = 0;
+    for (int base = 0; base < B; base += 32) {
+      int x = base + lane < B ? pre[base + lane + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (base + lane < B) pre[base + lane + 1] = carry + x;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) pre[0] = 0;
+  }
+  __syncthreads();
+  const int64_t T = pre[B];
+  const int64_t Wt = (int64_t)gridDim.x * kW;
+  const float kLn2 = 0.6931471805599453f;
+
+  if (warp == kW) {
+    // ============================ producer warp ===============================
+    constexpr int kIssue = 8;
+    static_assert(kNS % kIssue == 0 && 32 % kIssue == 0 && kIssue % kW == 0, "issue batch must divide the ring");
+    if (T == 0) return;
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+    const uint64_t policy = l2_policy_evict_first();
+    int64_t sh_start[kW];
+    int sh_len[kW];
+    int max_len = 0;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) {
+      const int64_t k = (int64_t)blockIdx.x * kW + w;
+      sh_start[w] = share_start(k, T, Wt);
+      sh_len[w] = (int)(share_start(k + 1, T, Wt) - sh_start[w]);
+      max_len = max(max_len, sh_len[w]);
+    }
+    const int n_issue = max_len * kW;
+    // block index of issue slot i; -2 when the slot lies past its warp's share
+    auto entry = [&](int i) -> long long {
+      if (i >= n_issue) return -2;
+      const int w = i % kW, j = i / kW;
+      int64_t s0 = sh_start[0];
+      int ln = sh_len[0];
+#pragma unroll
+      for (int ww = 1; ww < kW; ++ww)
+        if (w == ww) {
+          s0 = sh_start[ww];
+          ln = sh_len[ww];
+        }
+      if (j >= ln) return -2;
+      const int f = (int)(s0 + j);
+      const int r = find_request(pre, B, f);
+      const int nb = (pre[r + 1] - pre[r]) / Hkv;
+      const int off = f - pre[r];
+      const int h = off / nb;
+      const int pg = lo + (off - h * nb);
+      if (kPaged) return (long long)block_index<true>(p, r, h, (long long)p.table[(size_t)r * p.cols + pg]);
+      return (long long)block_index<false>(p, r, h, pg);
+    };
+    long long tcur = entry(lane);
+    long long tnxt = entry(32 + lane);
+    bool aborted = false;
+    for (int i0 = 0; i0 < n_issue; i0 += kIssue) {
+      if ((i0 & 31) == 0 && i0 > 0) {
+        tcur = tnxt;
+        tnxt = entry(i0 + 32 + lane);
+      }
+      const long long e = __shfl_sync(0xffffffffu, tcur, (i0 + (lane & (kIssue - 1))) & 31);
+      const int i = i0 + lane;
+      if (lane < kIssue && e != -2) {
+        const int st = i & (kNS - 1);
+        if (i >= kNS && !mbar_wait_bounded(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kTimeoutNs)) {
+          if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
+          aborted = true;
+        }
+        if (!aborted) issue_page(p, &tmk, &tmv, base_s, meta_p, meta_s, full_s + 8 * st, st, e, policy);
+      }
+      if (__any_sync(0xffffffffu, aborted)) break;
+    }
+    return;  // the producer takes no part in the epilogue
+  }
+
+  // ============================ consumer warps ===============================
+  const int g = lane >> 2, c = lane & 3;
+  {  // pairs without pages in the window still need an output: zeros (LSE -inf)
+    const int pairs = B * Hkv;
+    const int p_lo = (int)((int64_t)blockIdx.x * pairs / gridDim.x);
+    const int p_hi = (int)((int64_t)(blockIdx.x + 1) * pairs / gridDim.x);
+    for (int pr = p_lo + warp; pr < p_hi; pr += kW) {
+      const int r = pr / Hkv, h = pr % Hkv;
+      if (pre[r + 1] != pre[r]) continue;
+      for (int idx = lane; idx < p.G * kD; idx += 32)
+        write_final(p, (size_t)r * p.Hq + (size_t)h * p.G + (idx >> 7), idx & (kD - 1), 0.f, -INFINITY);
+    }
+  }
+  if (T == 0) return;
+  const int64_t k = (int64_t)blockIdx.x * kW + warp;
+  const int64_t f_begin = share_start(k, T, Wt);
+  const int len_w = (int)(share_start(k + 1, T, Wt) - f_begin);
+  const StageOffsets off(lane);
+  QueryFrag qf;
+  WarpState ws;
+  ws.reset();
+  int r = 0, h = 0, nb = 1, len_eff = 0;
+  int64_t pair_P = 0, pair_end = -1, piece_f0 = 0;
+  bool first_piece = true;
+  for (int j = 0; j < len_w; ++j) {
+    const int64_t f = f_begin + j;
+    if (f >= pair_end) {  // a new (request, kv head) piece starts
+      r = find_request(pre, B, (int)f);
+      nb = (pre[r + 1] - pre[r]) / Hkv;
+      h = (int)((f - pre[r]) / nb);
+      pair_P = pre[r] + (int64_t)h * nb;
+      pair_end = pair_P + nb;
+      piece_f0 = f;
+      window_pages<kPaged>(p, r, lo, hi_cap, &len_eff);
+      qf.load(p, r, h, lane);
+    }
+    const int i = j * kW + warp;
+    const int st = i & (kNS - 1);
+    if (!mbar_wait_bounded(full_s + 8 * st, (uint32_t)((i / kNS) & 1), kTimeoutNs)) {
+      if (lane == 0 && p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
+      return;
+    }
+    StageInfo si;
+    if (read_stage_info(meta_p, st, si)) {
+      consume_page<0>(base_s + st * kStageBytes, off, empty_s + 8 * st, lane, si, qf, p.qk_scale_log2,
+                      (lo + (int)(f - pair_P)) * kPage, len_eff, ws);
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_s + 8 * st);
+    }
+    if (f + 1 != pair_end && j + 1 != len_w) continue;
+
+    // ---- close the piece ------------------------------------------------------------
+    float l = ws.l_run;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    // normaliser / max of the queries 2c, 2c+1 of this thread's accumulator columns
+    const float l0 = __shfl_sync(0xffffffffu, l, 8 * c), l1 = __shfl_sync(0xffffffffu, l, 8 * c + 4);
+    const float m0 = __shfl_sync(0xffffffffu, ws.m_run, 8 * c), m1 = __shfl_sync(0xffffffffu, ws.m_run, 8 * c + 4);
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    const float lse0 = l0 > 0.f ? (m0 + log2f(l0)) * kLn2 : -INFINITY;
+    const float lse1 = l1 > 0.f ? (m1 + log2f(l1)) * kLn2 : -INFINITY;
+    const size_t row0 = (size_t)r * p.Hq + (size_t)h * p.G;
+    if (piece_f0 == pair_P && f + 1 == pair_end) {  // the whole pair: final output
+#pragma unroll
+      for (int i2 = 0; i2 < 8; ++i2) {
+        const int d = 16 * i2 + 2 * g;
+        if (2 * c < p.G) {
+          write_final(p, row0 + 2 * c, d, ws.acc[i2][0] * inv0, lse0);
+          write_final(p, row0 + 2 * c, d + 1, ws.acc[i2][2] * inv0, lse0);
+        }
+        if (2 * c + 1 < p.G) {
+          write_final(p, row0 + 2 * c + 1, d, ws.acc[i2][1] * inv1, lse1);
+          write_final(p, row0 + 2 * c + 1, d + 1, ws.acc[i2][3] * inv1, lse1);
+        }
+      }
+    } else {
+      // partial slot of this warp: O [Wt][2][G][kD], LSE [Wt][2][G]
+      const size_t slot = ((size_t)k * 2 + (first_piece ? 0 : 1)) * p.G;
+#pragma unroll
+      for (int i2 = 0; i2 < 8; ++i2) {
+        const int d = 16 * i2 + 2 * g;
+        if (2 * c < p.G) {
+          p.part_o[(slot + 2 * c) * kD + d] = ws.acc[i2][0] * inv0;
+          p.part_o[(slot + 2 * c) * kD + d + 1] = ws.acc[i2][2] * inv0;
+        }
+        if (2 * c + 1 < p.G) {
+          p.part_o[(slot + 2 * c + 1) * kD + d] = ws.acc[i2][1] * inv1;
+          p.part_o[(slot + 2 * c + 1) * kD + d + 1] = ws.acc[i2][3] * inv1;
+        }
+      }
+      const float lq = __shfl_sync(0xffffffffu, l, (4 * lane) & 31);
+      const float mq = __shfl_sync(0xffffffffu, ws.m_run, (4 * lane) & 31);
+      if (lane < p.G) p.part_lse[slot + lane] = lq > 0.f ? (mq + log2f(lq)) * kLn2 : -INFINITY;
+      const int64_t k0 = share_of(pair_P, T, Wt), k1 = share_of(pair_end - 1, T, Wt);
+      const unsigned contributors = (unsigned)(k1 - k0 + 1);
+      const int pair_id = r * Hkv + h;
+      __threadfence();
+      __syncwarp();
+      unsigned ticket = 0;
+      if (lane == 0) ticket = atomicAdd(p.counters + pair_id, 1u);
+      ticket = __shfl_sync(0xffffffffu, ticket, 0);
+      if (ticket == contributors - 1) {  // last contributor: merge the pair
+        __threadfence();
+        const bool k0_first = share_start(k0, T, Wt) == pair_P;
+        for (int qg = 0; qg < p.G; ++qg) {
+          float M = -INFINITY;
+          for (int64_t kk = k0; kk <= k1; ++kk) {
+            const size_t sl = ((size_t)kk * 2 + ((kk == k0 && !k0_first) ? 1 : 0)) * p.G + qg;
+            M = fmaxf(M, __ldcg(p.part_lse + sl));
+          }
+          float W = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+          if (M != -INFINITY) {
+            for (int64_t kk = k0; kk <= k1; ++kk) {
+              const size_t sl = ((size_t)kk * 2 + ((kk == k0 && !k0_first) ? 1 : 0)) * p.G + qg;
+              const float lse = __ldcg(p.part_lse + sl);
+              if (lse == -INFINITY) continue;
+              const float w = expf(lse - M);
+              W += w;
+              const float* src = p.part_o + sl * kD;
+              o0 = fmaf(w, __ldcg(src + lane), o0);
+              o1 = fmaf(w, __ldcg(src + lane + 32), o1);
+              o2 = fmaf(w, __ldcg(src + lane + 64), o2);
+              o3 = fmaf(w, __ldcg(src + lane + 96), o3);
+            }
+          }
+          const float inv = W > 0.f ? 1.f / W : 0.f;
+          const float lse_out = W > 0.f ? M + logf(W) : -INFINITY;
+          write_final(p, row0 + qg, lane, o0 * inv, lse_out);
+          write_final(p, row0 + qg, lane + 32, o1 * inv, lse_out);
+          write_final(p, row0 + qg, lane + 64, o2 * inv, lse_out);
+          write_final(p, row0 + qg, lane + 96, o3 * inv, lse_out);
+        }
+        if (lane == 0) p.counters[pair_id] = 0u;  // leave the ticket clean for the next call
+      }
+    }
+    first_piece = false;
+    ws.reset();
+  }
+}
+
 // ---------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------
@@ -590,8 +889,8 @@ struct Shape {
   int warps, stages, min_blocks;
 };
 using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
-constexpr Shape kShapes[] = {{4, 16, 3}, {4, 8, 4}, {8, 16, 2}};
-constexpr int kNumShapes = 3;
+constexpr Shape kShapes[] = {{4, 16, 3}, {8, 16, 2}};
+constexpr int kNumShapes = 2;
 constexpr int kDefaultShape = 0;
 
 template <bool kPaged, int kSi, int kMode>
@@ -611,17 +910,27 @@ static DecodeKernelFn kernel_mode(int mode) {
 
 template <bool kPaged>
 static DecodeKernelFn kernel_for(int shape, int mode) {
-  switch (shape) {
-    case 1: return kernel_mode<kPaged, 1>(mode);
-    case 2: return kernel_mode<kPaged, 2>(mode);
-    default: return kernel_mode<kPaged, 0>(mode);
-  }
+  return shape == 1 ? kernel_mode<kPaged, 1>(mode) : kernel_mode<kPaged, 0>(mode);
+}
+
+template <bool kPaged, int kSi>
+__host__ DecodeKernelFn balanced_inst() {
+  constexpr Shape sh = kShapes[kSi];
+  return decode_balanced_kernel<kPaged, sh.warps, sh.stages, sh.min_blocks>;
+}
+
+template <bool kPaged>
+static DecodeKernelFn balanced_for(int shape) {
+  return shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0>();
 }
 
 static int smem_bytes(int shape) {
   const Shape sh = kShapes[shape];
   return 1024 + sh.stages * (kStageBytes + kMetaBytes + 16);
 }
+
+// the balanced kernel adds its per-request prefix table
+static int smem_balanced(int shape, int batch) { return smem_bytes(shape) + ((4 * (batch + 1) + 15) & ~15); }
 
 // FLASHSPEC_DEBUG_MODE (profiling only, results are wrong when set): 1 = skip the math,
 // 2 = data movement only.
@@ -655,6 +964,9 @@ static int configure_kernel(int device, int shape) {
     if (cudaFuncSetAttribute(kernel_for<kPaged>(shape, mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem_bytes(shape)) != cudaSuccess)
       return FS_ERR_CUDA;
+  if (cudaFuncSetAttribute(balanced_for<kPaged>(shape), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem_balanced(shape, kMaxSKBatch)) != cudaSuccess)
+    return FS_ERR_CUDA;
   done[kPaged][shape][device] = true;
   return FS_OK;
 }
@@ -754,6 +1066,75 @@ static int resolve_splits(const FsDecodeArgs* a, int device, int shape) {
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Plan of one call: the balanced kernel on `ctas` CTAs, or the split kernel with `splits`.
+struct Plan {
+  bool balanced;
+  int splits;
+  int ctas;
+};
+
+static int balanced_per_sm(int device, int shape, int batch) {
+  static int cached[kNumShapes][kMaxDevices][16] = {};  // by 512-byte bucket of the prefix table
+  static std::mutex mu;
+  const int smem = smem_balanced(shape, batch);
+  int bucket = (smem - smem_bytes(shape)) / 512;
+  if (bucket > 15) bucket = 15;
+  std::lock_guard<std::mutex> lock(mu);
+  int& c = cached[shape][device][bucket];
+  if (c == 0) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, balanced_for<true>(shape), (kShapes[shape].warps + 1) * 32,
+                                                      smem_bytes(shape) + (bucket + 1) * 512) != cudaSuccess ||
+        per_sm <= 0)
+      per_sm = 1;
+    c = per_sm;
+  }
+  return c;
+}
+
+// FLASHSPEC_DECODE_KERNEL=split|balanced forces a kernel (profiling, tests).
+static int kernel_override() {
+  const char* v = getenv("FLASHSPEC_DECODE_KERNEL");
+  if (v == nullptr) return 0;
+  if (strcmp(v, "split") == 0) return 1;
+  if (strcmp(v, "balanced") == 0) return 2;
+  return 0;
+}
+
+// An explicit num_splits selects the split kernel.  Otherwise the balanced kernel runs,
+// unless each (request, kv head) pair would be shared by more than 16 warps (few very
+// long pairs): their merges would then sit on the critical path, and the split kernel
+// with one-wave splits does better.
+static Plan make_plan(const FsDecodeArgs* a, int device, int shape) {
+  Plan pl{false, 1, 0};
+  const int ov = kernel_override();
+  const int64_t pairs = (int64_t)a->batch * a->kv_heads;
+  const int64_t maxp = max_pages_of(a);
+  const int warps = kShapes[shape].warps;
+  bool balanced = a->num_splits <= 0 && a->batch <= kMaxSKBatch && maxp > 0 && pairs * maxp < (1ll << 31);
+  if (balanced) {
+    const int64_t slots = (int64_t)balanced_per_sm(device, shape, a->batch) * device_sm_count(device);
+    const int64_t t_est = pairs * maxp;
+    pl.ctas = (int)std::max<int64_t>(1, std::min<int64_t>(slots, t_est / (warps * 4)));
+    const int64_t contributors = (int64_t)pl.ctas * warps / pairs + 1;
+    if (contributors > 16 && ov != 2) balanced = false;
+    if (ov == 1) balanced = false;
+  }
+  if (balanced) {
+    pl.balanced = true;
+    pl.splits = 0;
+  } else {
+    pl.splits = resolve_splits(a, device, shape);
+  }
+  return pl;
+}
+
+static size_t workspace_balanced(const FsDecodeArgs* a, int ctas, int shape) {
+  const size_t G = (size_t)(a->q_heads / a->kv_heads);
+  const size_t slots = (size_t)ctas * kShapes[shape].warps * 2 * G;
+  return align256(slots * kD * 4) + align256(slots * 4);
+}
+
 static size_t workspace_for(const FsDecodeArgs* a, int splits) {
   if (splits <= 1) return 0;
   const size_t G = (size_t)(a->q_heads / a->kv_heads);
@@ -799,10 +1180,11 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
   const int shape = shape_choice();
   if ((st = configure_kernel<kPaged>(device, shape)) != FS_OK) return st;
-  const int splits = resolve_splits(a, device, shape);
-  const size_t need = workspace_for(a, splits);
+  if ((st = configure_kernel<true>(device, shape)) != FS_OK) return st;
+  const Plan pl = make_plan(a, device, shape);
+  const size_t need = pl.balanced ? workspace_balanced(a, pl.ctas, shape) : workspace_for(a, pl.splits);
   if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need)) return FS_ERR_WORKSPACE;
-  if (splits > 1 && (a->tickets == nullptr || a->ticket_count < (int64_t)a->batch * a->kv_heads))
+  if ((pl.balanced || pl.splits > 1) && (a->tickets == nullptr || a->ticket_count < (int64_t)a->batch * a->kv_heads))
     return FS_ERR_WORKSPACE;
 
   const uint64_t rows = kPaged ? (uint64_t)a->num_blocks * a->kv_heads * kPage
@@ -827,7 +1209,7 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.Hq = a->q_heads;
   p.Hkv = a->kv_heads;
   p.G = a->q_heads / a->kv_heads;
-  p.S = splits;
+  p.S = pl.balanced ? 1 : pl.splits;
   p.cols = a->table_cols;
   p.num_blocks = a->num_blocks;
   p.max_seq_len = a->max_seq_len;
@@ -835,18 +1217,25 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.page_end = a->page_end;
   p.zp_count = kPaged ? a->num_blocks * a->kv_heads : (int64_t)a->batch * a->kv_heads * a->num_blocks;
   p.qk_scale_log2 = a->sm_scale * 1.4426950408889634f;
-  if (splits > 1) {
+  if (need > 0) {
     const size_t G = (size_t)p.G;
-    const size_t units = (size_t)a->batch * a->kv_heads * splits * G;
+    const size_t units = pl.balanced ? (size_t)pl.ctas * kShapes[shape].warps * 2 * G
+                                     : (size_t)a->batch * a->kv_heads * pl.splits * G;
     uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
     p.part_o = reinterpret_cast<float*>(ws);
     p.part_lse = reinterpret_cast<float*>(ws + align256(units * kD * 4));
-    p.counters = reinterpret_cast<unsigned*>(a->tickets);
   }
-  const int64_t grid = (int64_t)a->batch * a->kv_heads * splits;
-  if (grid >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
-  kernel_for<kPaged>(shape, debug_mode())<<<(unsigned)grid, (kShapes[shape].warps + 1) * 32, smem_bytes(shape),
-                                     reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
+  p.counters = reinterpret_cast<unsigned*>(a->tickets);
+  const int threads = (kShapes[shape].warps + 1) * 32;
+  if (pl.balanced) {
+    balanced_for<kPaged>(shape)<<<(unsigned)pl.ctas, threads, smem_balanced(shape, a->batch),
+                                  reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
+  } else {
+    const int64_t grid = (int64_t)a->batch * a->kv_heads * pl.splits;
+    if (grid >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
+    kernel_for<kPaged>(shape, debug_mode())<<<(unsigned)grid, threads, smem_bytes(shape),
+                                              reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
+  }
   return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
 }
 
@@ -860,9 +1249,11 @@ int fs_decode_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* spli
   if (st != FS_OK) return st;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
-  const int s = fsb::resolve_splits(a, device, fsb::shape_choice());
-  *bytes = fsb::workspace_for(a, s);
-  if (splits_out) *splits_out = s;
+  const int shape = fsb::shape_choice();
+  if ((st = fsb::configure_kernel<true>(device, shape)) != FS_OK) return st;
+  const fsb::Plan pl = fsb::make_plan(a, device, shape);
+  *bytes = pl.balanced ? fsb::workspace_balanced(a, pl.ctas, shape) : fsb::workspace_for(a, pl.splits);
+  if (splits_out) *splits_out = pl.balanced ? 0 : pl.splits;
   return FS_OK;
 }
 

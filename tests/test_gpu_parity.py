@@ -346,3 +346,63 @@ def test_allocator_random_decode_loop_matches_oracle():
     if live:
         q = rng.standard_normal((len(live), H, D)).astype(np.float16)
         close(f.paged_quant_attention_cuda(dev(q), ga.to_cache(live)), O.paged_quant_attention(q, oa.to_cache(live)))
+
+
+# ---------------------------------------------------------------------------------
+# balanced (stream-K) kernel, forced through FLASHSPEC_DECODE_KERNEL
+# ---------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("kernel", ["balanced", "split"])
+@pytest.mark.parametrize("lens,hq,hkv", [([1, 16, 17, 250, 31, 512, 100], 8, 4),
+                                         ([2000, 3], 16, 2),      # few pairs: many warps share a pair
+                                         ([0, 40, 0, 7], 4, 4),   # empty requests
+                                         ([4096], 8, 8)])
+def test_decode_kernels_vs_oracle(monkeypatch, kernel, lens, hq, hkv):
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", kernel)
+    rng = np.random.default_rng(sum(lens) + hq)
+    q, oc = _random_paged(rng, len(lens), hq, hkv, [max(n, 1) for n in lens])
+    oc.lengths[:] = lens
+    out = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc))
+    ref = O.paged_quant_attention(q, oc)
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.all(out[i] == 0)
+        else:
+            close(out[i], ref[i])
+
+
+def test_balanced_kernel_deterministic_and_matches_split(monkeypatch):
+    rng = np.random.default_rng(21)
+    q, oc = _random_paged(rng, 5, 8, 2, [900, 13, 1500, 64, 333])
+    cache = _cache_dev(oc)
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "balanced")
+    a = fs().paged_quant_attention_cuda(dev(q), cache)
+    b = fs().paged_quant_attention_cuda(dev(q), cache)
+    assert torch.equal(a, b)
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "split")
+    c = fs().paged_quant_attention_cuda(dev(q), cache)
+    close(a, c.float().cpu().numpy(), atol=1e-3, rtol=1e-3)
+
+
+def test_balanced_page_windows_merge_equal_full(monkeypatch):
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "balanced")
+    rng = np.random.default_rng(8)
+    q, oc = _random_paged(rng, 3, 8, 8, [700, 333, 1200])
+    cache = _cache_dev(oc)
+    os_, ls_ = [], []
+    for lo, hi in [(0, 7), (7, 40), (40, 80)]:
+        o = torch.empty(q.shape, dtype=torch.float32, device="cuda")
+        lse = torch.empty(q.shape[:2], dtype=torch.float32, device="cuda")
+        fs().paged_quant_attention_cuda(dev(q), cache, page_range=(lo, hi), partial_out=(o, lse))
+        os_.append(o)
+        ls_.append(lse)
+    close(fs().merge_partials(torch.stack(os_), torch.stack(ls_)), O.paged_quant_attention(q, oc))
+
+
+def test_fused_balanced_vs_golden(monkeypatch):
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "balanced")
+    for name in ["fused_s129", "fused_s1500", "fused_nolen_s200"]:
+        g = load_golden(name)
+        lengths = dev(g["lengths"]) if "lengths" in g else None
+        close(fs().fused_dequant_attention_cuda(dev(g["q"]), qt_dev(g, "kq"), qt_dev(g, "vq"), lengths), g["out"])
