@@ -1045,7 +1045,7 @@ static int resolve_splits(const FsDecodeArgs* a, int device, int shape) {
   const int64_t cap = maxp / (kShapes[shape].warps * 4) > 1 ? maxp / (kShapes[shape].warps * 4) : 1;
   if (pairs <= 0 || maxp <= 0) return 1;
   int64_t best = 1;
-  if (pairs <= slots / 2) {
+  if (pairs <= slots) {  // one wave: split each pair as far as the wave allows
     best = slots / pairs;
   } else {
     double best_cost = 1e300;
@@ -1101,10 +1101,9 @@ static int kernel_override() {
   return 0;
 }
 
-// An explicit num_splits selects the split kernel.  Otherwise the balanced kernel runs,
-// unless each (request, kv head) pair would be shared by more than 16 warps (few very
-// long pairs): their merges would then sit on the critical path, and the split kernel
-// with one-wave splits does better.
+// An explicit num_splits selects the split kernel.  Otherwise the balanced kernel runs
+// when there are more (request, kv head) pairs than resident CTAs (then split CTAs come
+// in several unequal waves); with fewer pairs the split kernel fills exactly one wave.
 static Plan make_plan(const FsDecodeArgs* a, int device, int shape) {
   Plan pl{false, 1, 0};
   const int ov = kernel_override();
@@ -1116,8 +1115,11 @@ static Plan make_plan(const FsDecodeArgs* a, int device, int shape) {
     const int64_t slots = (int64_t)balanced_per_sm(device, shape, a->batch) * device_sm_count(device);
     const int64_t t_est = pairs * maxp;
     pl.ctas = (int)std::max<int64_t>(1, std::min<int64_t>(slots, t_est / (warps * 4)));
+    // With no more pairs than resident CTAs the split kernel already fills one wave with
+    // equal CTAs (measured faster); with few long pairs the merges would serialise.
+    const int64_t split_slots = resident_ctas(device, shape);
     const int64_t contributors = (int64_t)pl.ctas * warps / pairs + 1;
-    if (contributors > 16 && ov != 2) balanced = false;
+    if ((contributors > 16 || pairs <= split_slots) && ov != 2) balanced = false;
     if (ov == 1) balanced = false;
   }
   if (balanced) {
