@@ -184,37 +184,69 @@ struct StageOffsets {
   }
 };
 
-// Query fragment of one (request, kv head): thread (g,c) holds q[g][32c .. 32c+32) as the A
-// operand of S = Q K^T (logical k 2c,2c+1 | 2c+8,2c+9 of step j = head dim 32c+4j+0,1 | 2,3)
-// and qsum = the sum of the same fp16 values of row g.
+// Query fragment of one (request, kv head) for S = Q K^T on the int8 tensor cores.
+// Row g of q is held as 16-bit fixed point q ~= q16 * qscale (q16 = rint(q / qscale),
+// |q16| <= 32639, qscale = max|q| / 32639), split as q16 = 256 * hi + lo with signed
+// bytes hi, lo: two int8 MMAs give sum(q16 * s) exactly in int32.  Thread (g,c) holds
+// head dims [32c, 32c+32): word w covers dims 32c+4w .. 32c+4w+3, and k-step j uses
+// words 2j (logical k 4c..4c+3) and 2j+1 (logical k 16+4c..).  q16sum = sum of q16 over
+// the row (exact), used to apply the zero point once per page.
 struct QueryFrag {
-  uint32_t qh[16];
-  float qsum;
+  uint32_t hi[8], lo[8];
+  int q16sum;
+  float qscale;
   __device__ __forceinline__ void load(const DecodeParams& p, int b, int h, int lane) {
     const int g = lane >> 2, c = lane & 3;
-    qsum = 0.f;
+    uint32_t raw[16];
     if (g < p.G) {
       const uint4* qp =
           reinterpret_cast<const uint4*>(p.q + ((size_t)b * p.Hq + (size_t)h * p.G + g) * kD + 32 * c);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 v = __ldg(qp + i);
-        qh[4 * i + 0] = v.x;
-        qh[4 * i + 1] = v.y;
-        qh[4 * i + 2] = v.z;
-        qh[4 * i + 3] = v.w;
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&qh[i]));
-        qsum += f2.x + f2.y;
+        raw[4 * i] = v.x;
+        raw[4 * i + 1] = v.y;
+        raw[4 * i + 2] = v.z;
+        raw[4 * i + 3] = v.w;
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) qh[i] = 0u;
+      for (int i = 0; i < 16; ++i) raw[i] = 0u;
     }
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
-    qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&raw[i]));
+      amax = fmaxf(amax, fmaxf(fabsf(f2.x), fabsf(f2.y)));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float inv = amax > 0.f ? 32639.0f / amax : 0.f;
+    qscale = amax > 0.f ? amax / 32639.0f : 0.f;
+    int sum = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      uint32_t hw = 0u, lw = 0u;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&raw[2 * w + k]));
+        const float v2[2] = {f2.x, f2.y};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int q16 = __float2int_rn(v2[e] * inv);
+          const int qh = (q16 + 128) >> 8;
+          const int ql = q16 - (qh << 8);
+          sum += q16;
+          hw |= (uint32_t)(qh & 0xff) << (8 * (2 * k + e));
+          lw |= (uint32_t)(ql & 0xff) << (8 * (2 * k + e));
+        }
+      }
+      hi[w] = hw;
+      lo[w] = lw;
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    q16sum = sum;
   }
 };
 
@@ -242,9 +274,9 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
                                              const StageInfo& si, const QueryFrag& qf, float qk_scale_log2,
                                              int pos0, int len_eff, WarpState& ws) {
   const int c = lane & 3;
-  // ---- S = Q K^T: K bytes become 1024+u exactly (sign flip + exponent bytes); the
-  // (1024 + zp) offset is removed per page with qsum -------------------------------
-  float sa[2][4];
+  // ---- S = Q K^T on the int8 tensor cores, straight from the stored bytes s = u - 128:
+  // sum_d q16 * s = 256 * (hi . s) + (lo . s); u - zp = s + (128 - zp) is applied per page
+  int shi[2][4], slo[2][4];
   {
     uint4 kr[2][2];
 #pragma unroll
@@ -254,16 +286,16 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) sa[nt][k] = 0.f;
+      for (int k = 0; k < 4; ++k) shi[nt][k] = slo[nt][k] = 0;
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
+    for (int j = 0; j < 4; ++j) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const uint4 kv = kr[nt][jj >> 2];
-        const uint32_t w = (jj & 3) == 0 ? kv.x : (jj & 3) == 1 ? kv.y : (jj & 3) == 2 ? kv.z : kv.w;
-        const uint32_t x = w ^ 0x80808080u;
-        mma_16816(sa[nt], qf.qh[2 * jj], 0u, qf.qh[2 * jj + 1], 0u, prmt(x, kMagic, 0x5140u),
-                  prmt(x, kMagic, 0x5342u));
+        const uint4 kv = kr[nt][j >> 1];
+        const uint32_t b0 = (j & 1) ? kv.z : kv.x;
+        const uint32_t b1 = (j & 1) ? kv.w : kv.y;
+        mma_16832_s8(shi[nt], qf.hi[2 * j], 0u, qf.hi[2 * j + 1], 0u, b0, b1);
+        mma_16832_s8(slo[nt], qf.lo[2 * j], 0u, qf.lo[2 * j + 1], 0u, b0, b1);
       }
     }
   }
@@ -273,16 +305,16 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
   __syncwarp();
   if (lane == 0) mbar_arrive(empty_bar);  // the stage may be refilled now
   if (kMode == 1) {
-    ws.acc[0][0] += __uint_as_float((__float_as_uint(sa[0][0]) ^ vr[0] ^ vr[15]) & 0x007fffffu);
+    ws.acc[0][0] += __uint_as_float(((uint32_t)shi[0][0] ^ (uint32_t)slo[1][1] ^ vr[0] ^ vr[15]) & 0x007fffffu);
     return;
   }
-  const float f = si.ks * qk_scale_log2;
-  const float zq = -(1024.0f + (float)si.kz) * qf.qsum;
+  const float f = si.ks * qf.qscale * qk_scale_log2;
+  const int zc = (128 - (int)si.kz) * qf.q16sum;
   float t[4];
-  t[0] = (sa[0][0] + zq) * f;  // token 2c
-  t[1] = (sa[0][1] + zq) * f;  // token 2c+1
-  t[2] = (sa[1][0] + zq) * f;  // token 8+2c
-  t[3] = (sa[1][1] + zq) * f;  // token 9+2c
+  t[0] = (float)((shi[0][0] << 8) + slo[0][0] + zc) * f;  // token 2c
+  t[1] = (float)((shi[0][1] << 8) + slo[0][1] + zc) * f;  // token 2c+1
+  t[2] = (float)((shi[1][0] << 8) + slo[1][0] + zc) * f;  // token 8+2c
+  t[3] = (float)((shi[1][1] << 8) + slo[1][1] + zc) * f;  // token 9+2c
   if (pos0 + kPage > len_eff) {
     if (pos0 + 2 * c >= len_eff) t[0] = -INFINITY;
     if (pos0 + 2 * c + 1 >= len_eff) t[1] = -INFINITY;
