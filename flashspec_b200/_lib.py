@@ -119,7 +119,7 @@ SIGNATURES = {
     "fs_fused_decode": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
     "fs_paged_decode": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
     "fs_paged_decode_noalloc": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
-    "fs_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_void_p,
+    "fs_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int64, C.c_void_p,
                                     C.c_int32, C.c_void_p]),
     "fs_quantize_blocks": (C.c_int, [C.POINTER(FsQuantizeArgs), C.c_void_p]),
     "fs_page_update": (C.c_int, [C.POINTER(FsPageUpdateArgs), C.c_void_p]),

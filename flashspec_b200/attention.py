@@ -254,7 +254,7 @@ def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out_dtype: to
     out = torch.empty(o_parts.shape[1:], dtype=out_dtype, device=o_parts.device)
     code = {torch.float16: _lib.FS_F16, torch.float32: _lib.FS_F32}[out_dtype]
     with torch.cuda.device(o_parts.device):
-        _lib.check(_lib.load().fs_merge_partials(oc.data_ptr(), lc.data_ptr(), n, rows, d, out.data_ptr(), code,
+        _lib.check(_lib.load().fs_merge_partials(oc.data_ptr(), lc.data_ptr(), n, rows, d, 0, out.data_ptr(), code,
                                                  stream_of(o_parts.device)), "fs_merge_partials")
     return out
 

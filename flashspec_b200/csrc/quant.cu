@@ -165,19 +165,20 @@ __global__ void dequantize_pages_kernel(const int8_t* __restrict__ values, const
 }
 
 __global__ void merge_partials_kernel(const float* __restrict__ o, const float* __restrict__ lse, int n,
-                                      int64_t rows, int D, void* __restrict__ out, int out_dtype) {
+                                      int64_t rows, int D, int64_t stride, void* __restrict__ out, int out_dtype) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * D) return;
   const int64_t row = idx / D;
+  const int64_t so = stride ? stride : rows * D, sl = stride ? stride : rows;
   float M = -INFINITY;
-  for (int i = 0; i < n; ++i) M = fmaxf(M, lse[i * rows + row]);
+  for (int i = 0; i < n; ++i) M = fmaxf(M, lse[i * sl + row]);
   float W = 0.f, O = 0.f;
   if (M != -INFINITY) {
     for (int i = 0; i < n; ++i) {
-      const float l = lse[i * rows + row];
+      const float l = lse[i * sl + row];
       const float w = l == -INFINITY ? 0.f : expf(l - M);
       W += w;
-      O += w * o[i * rows * D + idx];
+      O += w * o[i * so + idx];
     }
   }
   const float r = W > 0.f ? O / W : 0.f;
@@ -249,7 +250,7 @@ int fs_dequantize_pages(const int8_t* values, const float* scale, const int16_t*
 }
 
 int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows, int32_t head_dim,
-                      void* out, int32_t out_dtype, void* stream) {
+                      int64_t part_stride, void* out, int32_t out_dtype, void* stream) {
   if (o_parts == nullptr || lse_parts == nullptr || out == nullptr || n_parts <= 0 || rows < 0 || head_dim <= 0)
     return FS_ERR_INVALID_ARGUMENT;
   if (out_dtype != FS_F16 && out_dtype != FS_F32) return FS_ERR_UNSUPPORTED;
@@ -258,7 +259,7 @@ int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_pa
   const int64_t blocks = (n + 255) / 256;
   if (blocks >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
   fsb::merge_partials_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      o_parts, lse_parts, n_parts, rows, head_dim, out, out_dtype);
+      o_parts, lse_parts, n_parts, rows, head_dim, part_stride < 0 ? 0 : part_stride, out, out_dtype);
   return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
 }
 

@@ -59,15 +59,22 @@ def _cuda_merge(o_parts, lse_parts, out_dtype):
 class SequenceShardedDecoder:
     """Decode one batch whose KV pages are split across the ranks of ``group``.
 
+    Default (CUDA) path per call: the rank's partial (O, LSE) is written by the decode
+    kernel straight into its slot of a preallocated [world, O | LSE] fp32 buffer, one
+    in-place ``all_gather_into_tensor`` fills the other slots (NCCL over NVLink), and
+    ``fs_merge_partials`` merges the strided slots into the fp16 output.  ``capture``
+    records that whole step as a CUDA graph so a step costs one graph replay.
+
     ``partial_fn(q, cache, (lo, hi)) -> (O, LSE)`` and ``merge_fn(O[N], LSE[N], dtype)``
-    default to the CUDA kernels; they are parameters so the collective logic can run
-    on CPU ranks (gloo) in tests."""
+    replace the CUDA steps (then the generic list all-gather is used); tests run the
+    collective logic on CPU ranks (gloo) that way."""
 
     def __init__(self, group: Optional[dist.ProcessGroup] = None,
-                 partial_fn: Callable = _cuda_partial, merge_fn: Callable = _cuda_merge):
+                 partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None):
         self.group = group
         self.partial_fn = partial_fn
         self.merge_fn = merge_fn
+        self._bufs = {}
 
     @property
     def world(self) -> int:
@@ -81,11 +88,64 @@ class SequenceShardedDecoder:
         return page_window(n_pages, self.rank, self.world)
 
     def __call__(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
-        o, lse = self.partial_fn(q, cache, self.window(n_pages))
+        if self.partial_fn is None and self.merge_fn is None and q.is_cuda:
+            return self._cuda_call(q, cache, n_pages, out_dtype)
+        pf = self.partial_fn or _cuda_partial
+        mf = self.merge_fn or _cuda_merge
+        o, lse = pf(q, cache, self.window(n_pages))
         if self.world == 1:
-            return self.merge_fn(o[None], lse[None], out_dtype)
+            return mf(o[None], lse[None], out_dtype)
         o_all = [torch.empty_like(o) for _ in range(self.world)]
         lse_all = [torch.empty_like(lse) for _ in range(self.world)]
         dist.all_gather(o_all, o.contiguous(), group=self.group)
         dist.all_gather(lse_all, lse.contiguous(), group=self.group)
-        return self.merge_fn(torch.stack(o_all), torch.stack(lse_all), out_dtype)
+        return mf(torch.stack(o_all), torch.stack(lse_all), out_dtype)
+
+    def _cuda_call(self, q, cache, n_pages, out_dtype):
+        import ctypes as C
+
+        from . import _lib
+        from .attention import paged_quant_attention_cuda
+        from .quant import stream_of
+
+        b, hq, d = q.shape
+        rows = b * hq
+        slot = (rows * d + rows + 63) // 64 * 64  # floats per rank: O then LSE, 256-byte aligned
+        key = (q.device, b, hq, d, self.world)
+        bufs = self._bufs.get(key)
+        if bufs is None:
+            mine = torch.empty((slot,), dtype=torch.float32, device=q.device)
+            gather = torch.empty((self.world, slot), dtype=torch.float32, device=q.device) if self.world > 1 else None
+            bufs = self._bufs[key] = (mine, gather)
+        mine, gather = bufs
+        o = mine[: rows * d].view(b, hq, d)
+        lse = mine[rows * d: rows * d + rows].view(b, hq)
+        paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages), partial_out=(o, lse))
+        if self.world > 1:  # out of place: the send buffer is not a view of the receive buffer
+            dist.all_gather_into_tensor(gather.view(-1), mine, group=self.group)
+        else:
+            gather = mine.view(1, slot)
+        out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+        code = {torch.float16: _lib.FS_F16, torch.float32: _lib.FS_F32}[out_dtype]
+        base = gather.data_ptr()
+        _lib.check(_lib.load().fs_merge_partials(base, base + 4 * rows * d, self.world, rows, d, slot, out.data_ptr(),
+                                                 code, stream_of(q.device)), "fs_merge_partials")
+        return out
+
+    def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16):
+        """Record the decode step of a single-rank group (partial kernel + merge) as a CUDA
+        graph over the given tensors; returns ``(replay, out)`` where ``replay()`` re-runs
+        the step on the current contents of q / cache and refreshes ``out``.  Steps with a
+        collective are not captured (groups of more than one rank run eagerly)."""
+        if self.world > 1:
+            raise ValueError("capture() is for single-rank groups; multi-rank steps run eagerly")
+        side = torch.cuda.Stream(device=q.device)
+        side.wait_stream(torch.cuda.current_stream(q.device))
+        with torch.cuda.stream(side):
+            for _ in range(3):  # workspaces, kernel attributes, NCCL communicator set-up
+                self(q, cache, n_pages, out_dtype)
+        torch.cuda.current_stream(q.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self(q, cache, n_pages, out_dtype)
+        return graph.replay, out

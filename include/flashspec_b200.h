@@ -119,12 +119,15 @@ int fs_paged_decode(const FsDecodeArgs* args, void* stream);
 int fs_paged_decode_noalloc(const FsDecodeArgs* args, void* stream);
 
 /* Log-sum-exp merge of n_parts partial results (split-K partials, or per-GPU
- * shards gathered over NVLink).  o_parts fp32 [n_parts, rows, head_dim],
- * lse_parts fp32 [n_parts, rows]; writes out [rows, head_dim] as out_dtype
- * (FS_F16 or FS_F32).  Rows whose partials are all empty produce 0.
+ * shards gathered over NVLink).  Part i's O is o_parts + i*S ([rows, head_dim] fp32)
+ * and its LSE lse_parts + i*S' ([rows] fp32), where S = part_stride and S' =
+ * part_stride (both in floats) when part_stride > 0 -- e.g. parts packed as
+ * [O | LSE] slots of one all-gather buffer -- and S = rows*head_dim, S' = rows when
+ * part_stride == 0 (dense stacks).  Writes out [rows, head_dim] as out_dtype (FS_F16
+ * or FS_F32); rows whose partials are all empty produce 0.
  * Same math as _combine_splits_kernel (src/flashspec/triton_fused.py:446-503). */
 int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows,
-                      int32_t head_dim, void* out, int32_t out_dtype, void* stream);
+                      int32_t head_dim, int64_t part_stride, void* out, int32_t out_dtype, void* stream);
 
 /* Affine INT8 quantization of x [n_lead, seq_len, head_dim] (dtype x_dtype,
  * contiguous) in blocks of block_size tokens, zero-padding the last block:

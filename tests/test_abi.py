@@ -38,7 +38,7 @@ def test_calls_without_gpu_fail_cleanly():
 
     lib = _lib.load()
     assert lib.fs_page_update(None, None) == 1  # invalid argument, no CUDA call
-    assert lib.fs_merge_partials(None, None, 1, 1, 1, None, 0, None) == 1
+    assert lib.fs_merge_partials(None, None, 1, 1, 1, 0, None, 0, None) == 1
     a = _lib.FsDecodeArgs()
     assert lib.fs_paged_decode(C.byref(a), None) == 1
 

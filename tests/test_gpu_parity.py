@@ -406,3 +406,20 @@ def test_fused_balanced_vs_golden(monkeypatch):
         g = load_golden(name)
         lengths = dev(g["lengths"]) if "lengths" in g else None
         close(fs().fused_dequant_attention_cuda(dev(g["q"]), qt_dev(g, "kq"), qt_dev(g, "vq"), lengths), g["out"])
+
+
+def test_sequence_sharded_decoder_single_rank_and_graph_replay():
+    from flashspec_b200.dist import SequenceShardedDecoder
+
+    rng = np.random.default_rng(12)
+    q, oc = _random_paged(rng, 2, 16, 2, [900, 301])
+    cache = _cache_dev(oc)
+    qd = dev(q)
+    dec = SequenceShardedDecoder()
+    out = dec(qd, cache, cache.block_table.shape[1])
+    close(out, O.paged_quant_attention(q, oc))
+    replay, gout = dec.capture(qd, cache, cache.block_table.shape[1])
+    qd.copy_(dev(rng.standard_normal(q.shape).astype(np.float16)))  # new query, same graph
+    replay()
+    torch.cuda.synchronize()
+    close(gout, O.paged_quant_attention(qd.cpu().numpy(), oc))
