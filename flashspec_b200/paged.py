@@ -244,19 +244,29 @@ def _as_pool(qt) -> QuantizedTensor:
                            int(qt.block_size), tuple(qt.original_shape))
 
 
-@dataclass
 class _Request:
-    pages: List[int]
-    length: int
+    """Host record of one live request: its row in the allocator's page table and its
+    token count."""
+
+    __slots__ = ("slot", "length", "_owner")
+
+    def __init__(self, slot: int, length: int, owner: "PagedKVAllocator"):
+        self.slot, self.length, self._owner = slot, length, owner
+
+    @property
+    def pages(self) -> List[int]:
+        o = self._owner
+        return o._ptab[self.slot, : o._npages[self.slot]].tolist()
 
 
 class PagedKVAllocator:
     """Device-resident version of the reference PagedKVAllocator (paged.py:17-255).
 
-    The pool lives in HBM; the bookkeeping (free list, per-request page lists) is on
-    the host exactly as in the reference, and every data write is one batched
-    ``fs_page_update`` launch.  The free list is a min-heap: allocation takes the
-    lowest free page, which is what the reference's sorted list + pop(0) does."""
+    The pool lives in HBM; the bookkeeping is on the host: a min-heap free list
+    (allocation takes the lowest free page, which is what the reference's sorted list +
+    pop(0) does) and a slot-indexed numpy page table (row = live request, -1 padded), so
+    ``to_cache`` and single-token ``append_batch`` are a few numpy operations rather than
+    a Python loop per request.  Every data write is one batched ``fs_page_update``."""
 
     def __init__(self, *, capacity_blocks: int, heads: int, head_dim: int, block_size: int = 16,
                  device="cuda", dtype: torch.dtype = torch.float32) -> None:
@@ -278,6 +288,10 @@ class PagedKVAllocator:
         self.v_quant = empty_pool(self.capacity_blocks, self.heads, self.block_size, self.head_dim, self.device)
         self._free: List[int] = list(range(self.capacity_blocks))  # a valid min-heap
         self._requests: Dict[int, _Request] = {}
+        self._ptab = np.full((16, 16), -1, np.int64)  # [slot, logical page] -> physical page
+        self._npages = np.zeros(16, np.int64)
+        self._lens = np.zeros(16, np.int64)
+        self._free_slots: List[int] = list(range(16))
 
     # -- bookkeeping ----------------------------------------------------------------
     @property
@@ -293,6 +307,22 @@ class PagedKVAllocator:
         if not self._free:
             raise RuntimeError("PagedKVAllocator is out of physical pages")
         return heapq.heappop(self._free)
+
+    def _new_slot(self, pages_hint: int) -> int:
+        if not self._free_slots:
+            n = self._ptab.shape[0]
+            self._ptab = np.concatenate([self._ptab, np.full((n, self._ptab.shape[1]), -1, np.int64)], 0)
+            self._npages = np.concatenate([self._npages, np.zeros(n, np.int64)])
+            self._lens = np.concatenate([self._lens, np.zeros(n, np.int64)])
+            self._free_slots = list(range(2 * n - 1, n - 1, -1))
+        self._ensure_cols(pages_hint)
+        return self._free_slots.pop()
+
+    def _ensure_cols(self, cols: int) -> None:
+        if cols > self._ptab.shape[1]:
+            new = max(cols, 2 * self._ptab.shape[1])
+            pad = np.full((self._ptab.shape[0], new - self._ptab.shape[1]), -1, np.int64)
+            self._ptab = np.concatenate([self._ptab, pad], 1)
 
     def _validate_kv(self, k: torch.Tensor, v: torch.Tensor, *, batch_expected: Optional[int]) -> None:
         """paged.py:201-219."""
@@ -331,16 +361,21 @@ class PagedKVAllocator:
         need = (eff + self.block_size - 1) // self.block_size
         if len(self._free) < need:
             raise RuntimeError("PagedKVAllocator is out of physical pages")
+        slot = self._new_slot(need)
         pages = [self._allocate_block() for _ in range(need)]
-        items = np.zeros(need, ITEM_DTYPE)
+        self._ptab[slot, :] = -1
+        self._ptab[slot, :need] = pages
+        self._npages[slot] = need
+        self._lens[slot] = eff
         if need:
+            items = np.zeros(need, ITEM_DTYPE)
             starts = np.arange(need) * self.block_size
             items["page"] = pages
             items["src_t"] = starts
             items["n_rows"] = np.minimum(self.block_size, eff - starts)
             items["from_zero"] = 1
             page_update(items, k, v, self.k_quant, self.v_quant)
-        self._requests[request_id] = _Request(pages, eff)
+        self._requests[request_id] = _Request(slot, eff, self)
 
     def append_request(self, request_id: int, k_new: torch.Tensor, v_new: torch.Tensor) -> None:
         """paged.py:108-136."""
@@ -348,46 +383,65 @@ class PagedKVAllocator:
         self.append_batch([request_id], k_new, v_new)
 
     def append_batch(self, request_ids: Sequence[int], k_new: torch.Tensor, v_new: torch.Tensor) -> None:
-        """paged.py:138-144, batched: every touched page of every request is rewritten
-        by a single kernel launch.  Pages are allocated in the reference's order
-        (requests in order, tokens in order)."""
+        """paged.py:138-144, batched: every touched page of every request is rewritten by
+        one kernel launch.  Pages are allocated in the reference's order (requests in
+        order, tokens in order)."""
         ids = [int(r) for r in request_ids]
         self._validate_kv(k_new, v_new, batch_expected=len(ids))
         t = int(k_new.shape[2])
         reqs = [self._get(r) for r in ids]
-        need = sum(max(0, (r.length + t + self.block_size - 1) // self.block_size - len(r.pages)) for r in reqs)
-        if need > len(self._free):
+        slots = np.fromiter((r.slot for r in reqs), np.int64, len(reqs))
+        lens = self._lens[slots]
+        npg = self._npages[slots]
+        bs = self.block_size
+        need_pages = np.maximum(0, (lens + t + bs - 1) // bs - npg)
+        if int(need_pages.sum()) > len(self._free):
             raise RuntimeError("PagedKVAllocator is out of physical pages")
-        recs = []
-        for bi, req in enumerate(reqs):
-            ti = 0
-            while ti < t:
-                pos = req.length + ti
-                lb, off = divmod(pos, self.block_size)
-                if lb == len(req.pages):
-                    req.pages.append(self._allocate_block())
-                n = min(t - ti, self.block_size - off)
-                recs.append((req.pages[lb], bi, ti, off, n, 0, 0))
-                ti += n
-            req.length += t
-        page_update(np.array(recs, ITEM_DTYPE), k_new, v_new, self.k_quant, self.v_quant)
+        self._ensure_cols(int(((lens + t + bs - 1) // bs).max()) if len(ids) else 0)
+        if t == 1:  # decode step: one row into each tail page
+            off = lens % bs
+            lb = lens // bs
+            for i in np.nonzero(need_pages)[0]:  # new tail pages, lowest free first, request order
+                self._ptab[slots[i], lb[i]] = self._allocate_block()
+            self._npages[slots] = np.maximum(npg, lb + 1)
+            items = np.zeros(len(ids), ITEM_DTYPE)
+            items["page"] = self._ptab[slots, lb]
+            items["src_b"] = np.arange(len(ids))
+            items["dst_row"] = off
+            items["n_rows"] = 1
+        else:
+            recs = []
+            for bi, slot in enumerate(slots):
+                ti, ln = 0, int(self._lens[slot])
+                while ti < t:
+                    lb_, off_ = divmod(ln + ti, bs)
+                    if lb_ == self._npages[slot]:
+                        self._ptab[slot, lb_] = self._allocate_block()
+                        self._npages[slot] += 1
+                    n = min(t - ti, bs - off_)
+                    recs.append((int(self._ptab[slot, lb_]), bi, ti, off_, n, 0, 0))
+                    ti += n
+            items = np.array(recs, ITEM_DTYPE)
+        self._lens[slots] += t
+        for r in reqs:
+            r.length += t
+        page_update(items, k_new, v_new, self.k_quant, self.v_quant)
 
     def release_request(self, request_id: int) -> None:
         """paged.py:146-151: the pages return to the free list (not zeroed)."""
         req = self._requests.pop(int(request_id))
-        for p in req.pages:
+        for p in self._ptab[req.slot, : self._npages[req.slot]].tolist():
             heapq.heappush(self._free, p)
+        self._ptab[req.slot, :] = -1
+        self._npages[req.slot] = 0
+        self._lens[req.slot] = 0
+        self._free_slots.append(req.slot)
 
     # -- views ---------------------------------------------------------------------------
     def block_table_numpy(self, request_ids: Sequence[int]) -> Tuple[np.ndarray, np.ndarray]:
-        reqs = [self._get(r) for r in request_ids]
-        cols = max(1, max((len(r.pages) for r in reqs), default=0))
-        table = np.full((len(reqs), cols), -1, np.int64)
-        lens = np.empty((len(reqs),), np.int64)
-        for i, r in enumerate(reqs):
-            table[i, : len(r.pages)] = r.pages
-            lens[i] = r.length
-        return table, lens
+        slots = np.fromiter((self._get(r).slot for r in request_ids), np.int64, len(request_ids))
+        cols = max(1, int(self._npages[slots].max()) if len(slots) else 0)
+        return self._ptab[slots, :cols].copy(), self._lens[slots].copy()
 
     def to_cache(self, request_ids: Optional[Sequence[int]] = None) -> PagedKVCache:
         """paged.py:153-179: table/lengths in the given request order, -1 padded."""
