@@ -53,6 +53,7 @@ constexpr int kStageBytes = 2 * kPageBytes;  // K + V
 constexpr int kMetaBytes = 32;
 constexpr int kMaxG = 8;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint32_t kProducerSleepNs = 1000;  // suspend hint of the producer's free-stage waits
 
 struct DecodeParams {
   const __half* q;
@@ -452,7 +453,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       const int i = i0 + lane;
       if (lane < kIssue && i < n) {
         const int st = i & (kNS - 1);
-        if (i >= kNS && !mbar_wait_bounded(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kTimeoutNs)) {
+        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kProducerSleepNs, kTimeoutNs)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
@@ -653,8 +654,8 @@ __device__ __forceinline__ int window_pages(const DecodeParams& p, int r, int lo
   return max(0, min(np, hi_cap) - lo);
 }
 
-template <bool kPaged, int kW, int kNS, int kMinBlocks>
-__global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
+template <bool kPaged, int kW, int kNS, int kMaxRegs>
+__global__ void __maxnreg__(kMaxRegs)
     decode_balanced_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                            const DecodeParams p) {
   using L = SmemLayout<kW, kNS>;
@@ -758,7 +759,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       const int i = i0 + lane;
       if (lane < kIssue && e != -2) {
         const int st = i & (kNS - 1);
-        if (i >= kNS && !mbar_wait_bounded(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kTimeoutNs)) {
+        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kProducerSleepNs, kTimeoutNs)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
@@ -918,10 +919,10 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
 // FLASHSPEC_NUM_WARPS picks the shape by consumer-warp count (the reference's
 // num_warps knob, triton_utils.py:101-116); FLASHSPEC_KERNEL_SHAPE picks by index.
 struct Shape {
-  int warps, stages, min_blocks;
+  int warps, stages, min_blocks, max_regs;  // max_regs: register cap of the balanced kernel
 };
 using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
-constexpr Shape kShapes[] = {{4, 16, 3}, {8, 16, 2}};
+constexpr Shape kShapes[] = {{4, 16, 3, 128}, {8, 16, 2, 112}};
 constexpr int kNumShapes = 2;
 constexpr int kDefaultShape = 0;
 
@@ -948,7 +949,7 @@ static DecodeKernelFn kernel_for(int shape, int mode) {
 template <bool kPaged, int kSi>
 __host__ DecodeKernelFn balanced_inst() {
   constexpr Shape sh = kShapes[kSi];
-  return decode_balanced_kernel<kPaged, sh.warps, sh.stages, sh.min_blocks>;
+  return decode_balanced_kernel<kPaged, sh.warps, sh.stages, sh.max_regs>;
 }
 
 template <bool kPaged>

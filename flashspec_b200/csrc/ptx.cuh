@@ -59,6 +59,18 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
   return ok != 0;
 }
 
+// Bounded wait that suspends from the first attempt (for a warp whose latency does not
+// matter, e.g. a producer waiting for a free stage): leaves issue slots to the others.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint32_t bar, uint32_t parity, uint32_t hint_ns, uint64_t limit_ns) {
+  if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait_sleep(bar, parity, hint_ns)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
 // Bounded wait: gives up after ~limit_ns of wall time and returns false.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;

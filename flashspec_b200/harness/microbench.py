@@ -32,7 +32,7 @@ import torch
 from . import ncu_parse
 
 NOMINAL_HBM_GBS = 8000.0
-NCU_KERNEL_REGEX = {"cuda_paged": "decode_kernel", "cuda_fused": "decode_kernel", "dense": "."}
+NCU_KERNEL_REGEX = {"cuda_paged": "decode_", "cuda_fused": "decode_", "dense": "."}
 COUNTER_SECTIONS = ("WarpStateStats", "SchedulerStats", "MemoryWorkloadAnalysis", "SpeedOfLight", "Occupancy")
 
 
