@@ -254,16 +254,37 @@ struct QueryFrag {
 // Online-softmax state of one warp: running max (log2 domain, finite so exp2 never sees
 // inf - inf), this thread's share of the denominator, and the PV accumulator
 // acc[i][0..3] = O[d = 16i+2g (+1 for [2],[3])][query 2c | 2c+1].
+// The PV MMAs multiply P by 1024 + u (the exact fp16 form of the stored byte) rather than
+// by u - zp; z_run collects this thread's share of sum_t P16[g][t] * (1024 + zp_page) for
+// query row g, and fold_zero_point() subtracts it once, when the warp's pages are done.
 struct WarpState {
-  float m_run, l_run;
+  float m_run, l_run, z_run;
   float acc[8][4];
   __device__ __forceinline__ void reset() {
     m_run = -1.0e30f;
     l_run = 0.f;
+    z_run = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
       for (int k = 0; k < 4; ++k) acc[i][k] = 0.f;
+  }
+  // acc[.][0|2] belong to query 2c and acc[.][1|3] to query 2c+1, whose corrections sit
+  // (summed over the 4 lanes of a row) in lanes 8c and 8c+4.
+  __device__ __forceinline__ void fold_zero_point(int lane) {
+    float z = z_run;
+    z += __shfl_xor_sync(0xffffffffu, z, 1);
+    z += __shfl_xor_sync(0xffffffffu, z, 2);
+    const int c = lane & 3;
+    const float z0 = __shfl_sync(0xffffffffu, z, 8 * c), z1 = __shfl_sync(0xffffffffu, z, 8 * c + 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      acc[i][0] -= z0;
+      acc[i][1] -= z1;
+      acc[i][2] -= z0;
+      acc[i][3] -= z1;
+    }
+    z_run = 0.f;
   }
 };
 
@@ -330,6 +351,7 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
     const float alpha = ex2_approx(ws.m_run - m_new);
     ws.m_run = m_new;
     ws.l_run *= alpha;
+    ws.z_run *= alpha;
     const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
     const float a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
 #pragma unroll
@@ -346,15 +368,20 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
   ws.l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
   const uint32_t pb0 = pack_half2(pr[0] * si.vs, pr[1] * si.vs);
   const uint32_t pb1 = pack_half2(pr[2] * si.vs, pr[3] * si.vs);
+  {  // the zero point, applied per page to the exact fp16 P values the MMAs see
+    const float2 p01 = __half22float2(*reinterpret_cast<const __half2*>(&pb0));
+    const float2 p23 = __half22float2(*reinterpret_cast<const __half2*>(&pb1));
+    ws.z_run = fmaf(1024.f + (float)si.vz, (p01.x + p01.y) + (p23.x + p23.y), ws.z_run);
+  }
   // ---- O += P V: vr(chunk i, tokens 0-7 | 8-15) hold bytes
-  // [V[2c][d], V[2c][d+1], V[2c+1][d], V[2c+1][d+1]] with d = 16i + 2g ---------------
-  const uint32_t zv2 = (0x6400u + si.vz) * 0x10001u;
+  // [V[2c][d], V[2c][d+1], V[2c+1][d], V[2c+1][d+1]] with d = 16i + 2g; the stored byte
+  // is u - 128, so XOR 0x80 gives u and PRMT with exponent bytes 0x64 the fp16 1024 + u.
 #pragma unroll
   for (int i2 = 0; i2 < 8; ++i2) {
     const uint32_t x0 = vr[4 * (i2 >> 1) + 2 * (i2 & 1)] ^ 0x80808080u;
     const uint32_t x1 = vr[4 * (i2 >> 1) + 2 * (i2 & 1) + 1] ^ 0x80808080u;
-    mma_16816(ws.acc[i2], hsub2_u32(prmt(x0, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x0, kMagic, 0x5341u), zv2),
-              hsub2_u32(prmt(x1, kMagic, 0x5240u), zv2), hsub2_u32(prmt(x1, kMagic, 0x5341u), zv2), pb0, pb1);
+    mma_16816(ws.acc[i2], prmt(x0, kMagic, 0x5240u), prmt(x0, kMagic, 0x5341u), prmt(x1, kMagic, 0x5240u),
+              prmt(x1, kMagic, 0x5341u), pb0, pb1);
   }
 }
 
@@ -489,6 +516,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     }
     ws.l_run += __shfl_xor_sync(0xffffffffu, ws.l_run, 1);
     ws.l_run += __shfl_xor_sync(0xffffffffu, ws.l_run, 2);
+    ws.fold_zero_point(lane);
   }
 
   // ---- merge the consumer warps through shared memory ---------------------------
@@ -823,6 +851,7 @@ __global__ void __maxnreg__(kMaxRegs)
     if (f + 1 != pair_end && j + 1 != len_w) continue;
 
     // ---- close the piece ------------------------------------------------------------
+    ws.fold_zero_point(lane);
     float l = ws.l_run;
     l += __shfl_xor_sync(0xffffffffu, l, 1);
     l += __shfl_xor_sync(0xffffffffu, l, 2);
