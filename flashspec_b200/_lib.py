@@ -13,6 +13,7 @@ from pathlib import Path
 _LIB_PATH = Path(__file__).resolve().parent / "libflashspec_b200.so"
 
 FS_OK = 0
+FS_ERR_CUDA = 3
 FS_F16, FS_BF16, FS_F32 = 0, 1, 2
 FS_LAYOUT_CONTIGUOUS, FS_LAYOUT_PAGED = 0, 1
 FS_DEV_BAD_PAGE, FS_DEV_TIMEOUT = 1, 2
@@ -115,6 +116,7 @@ class FsPageUpdateArgs(C.Structure):
 SIGNATURES = {
     "fs_abi_version": (C.c_int, []),
     "fs_status_string": (C.c_char_p, [C.c_int]),
+    "fs_last_error_detail": (C.c_char_p, []),
     "fs_decode_workspace_size": (C.c_int, [C.POINTER(FsDecodeArgs), C.POINTER(C.c_size_t), C.POINTER(C.c_int32)]),
     "fs_fused_decode": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
     "fs_paged_decode": (C.c_int, [C.POINTER(FsDecodeArgs), C.c_void_p]),
@@ -157,4 +159,6 @@ def load() -> C.CDLL:
 def check(status: int, what: str) -> None:
     if status != FS_OK:
         msg = load().fs_status_string(status).decode()
+        if status == FS_ERR_CUDA:
+            msg += f" [{load().fs_last_error_detail().decode()}]"
         raise _STATUS_EXC.get(status, RuntimeError)(f"{what} failed: {msg} (status {status})")

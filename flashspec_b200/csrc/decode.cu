@@ -70,18 +70,25 @@ struct DecodeParams {
   float* part_lse;
   unsigned* counters;
   uint32_t* status;
+  unsigned long long* trace;  // profiling only: per-warp globaltimer stamps, usually null
   int B, Hq, Hkv, G, S, cols;
   int64_t num_blocks;
   int64_t max_seq_len;
   int64_t page_begin, page_end;
   int64_t zp_count;
   float qk_scale_log2;
+  int tier_ctas, skew;  // balanced kernel: CTAs per tier (the SM count) and the tier weight step
+  int piece_cost;       // balanced kernel: virtual pages charged per (request, kv head) pair
 };
 
 // Shared-memory plan of one CTA: a ring of kNS page stages (K 2 KB + V 2 KB, 1024-byte
 // aligned for the 128-byte TMA swizzle), 32 bytes of qparams per stage
 // (k_scale, v_scale, k zero-point word, v zero-point word, flags), and a full / empty
 // mbarrier pair per stage.  The warp merge at the end reuses the ring.
+// Pages the producer warp issues per loop trip (one lane each): 8, or 4 when 8 does not
+// divide the ring.
+__host__ __device__ constexpr int issue_batch(int stages) { return stages % 8 == 0 ? 8 : 4; }
+
 template <int kW, int kNS>
 struct SmemLayout {
   static constexpr int kStageRegion = kNS * kStageBytes;
@@ -89,7 +96,6 @@ struct SmemLayout {
   static constexpr int kBarRegion = kNS * 16;
   static constexpr int kMergeBytes = kW * (2 * kMaxG + kMaxG * kD) * 4;
   static_assert(kMergeBytes <= kStageRegion, "merge scratch reuses the stage ring");
-  static_assert((kNS & (kNS - 1)) == 0, "stage count must be a power of two");
   // Every stage must always be consumed by the same warp (page i -> warp i % kW, stage
   // i % kNS).  Otherwise a warp can wait on a stage's full barrier a whole phase early
   // and the parity test aliases with the previous phase.
@@ -458,7 +464,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     // ============================ producer warp ===============================
     // Pages are issued in batches of kIssue: lane j handles page i + j, so one warp
     // instruction issues kIssue TMA loads.
-    constexpr int kIssue = 8;
+    constexpr int kIssue = issue_batch(kNS);
     static_assert(kNS % kIssue == 0 && 32 % kIssue == 0, "issue batch must divide the ring");
     prefetch_tmap(&tmk);
     prefetch_tmap(&tmv);
@@ -479,8 +485,8 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       }
       const int i = i0 + lane;
       if (lane < kIssue && i < n) {
-        const int st = i & (kNS - 1);
-        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kProducerSleepNs, kTimeoutNs)) {
+        const int st = (int)((unsigned)i % kNS);
+        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (((unsigned)i / kNS) - 1u) & 1u, kProducerSleepNs, kTimeoutNs)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
@@ -499,8 +505,8 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     qf.load(p, b, h, lane);
     const StageOffsets off(lane);
     for (int i = warp; i < n; i += kW) {
-      const int st = i & (kNS - 1);
-      if (!mbar_wait_bounded(full_s + 8 * st, (uint32_t)((i / kNS) & 1), kTimeoutNs)) {
+      const int st = (int)((unsigned)i % kNS);
+      if (!mbar_wait_bounded(full_s + 8 * st, ((unsigned)i / kNS) & 1u, kTimeoutNs)) {
         if (lane == 0 && p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
         aborted = true;
         break;
@@ -646,8 +652,8 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
 // Balanced kernel (stream-K over pages): a persistent grid of C CTAs with kW consumer
 // warps each.  The flattened work space is every (request, kv head, page of the window)
 // in request-major order, T pages in total; consumer warp k of the Wt = C*kW warps owns
-// the contiguous share [k*T/Wt, (k+1)*T/Wt), so every warp streams the same number of
-// pages whatever the lengths.  Per-request page counts come from `lengths` on the device
+// a contiguous share of it (Shares below), so the warps stream equal amounts of work
+// whatever the lengths.  Per-request page counts come from `lengths` on the device
 // (a block-wide prefix sum at start), so the host never synchronises.  The producer warp
 // interleaves its CTA's kW shares through one ring (issue index i -> warp i % kW, step
 // i / kW, stage i % kNS).  A consumer warp closes a "piece" whenever its share crosses a
@@ -658,9 +664,148 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
 // ==================================================================================
 constexpr int kMaxSKBatch = 1536;  // requests whose prefix sums fit the shared-memory table
 
-__device__ __forceinline__ int64_t share_start(int64_t k, int64_t T, int64_t Wt) { return k * T / Wt; }
-// warp whose share contains flat page f
-__device__ __forceinline__ int64_t share_of(int64_t f, int64_t T, int64_t Wt) { return ((f + 1) * Wt - 1) / T; }
+// Division of the T flat pages between the Wt consumer warps.  A full grid places
+// `tiers` CTAs on every SM (CTA b in tier b / tier_ctas), and on B200 the CTAs of an SM
+// do not stream at the same rate: the first one resident on the SM gets its warps
+// issued first and finishes about 5% sooner than the second, which beats the third by
+// as much again.  A warp of tier t therefore gets weight 1024 - skew * t, and warp k's
+// share starts at floor(T * C(k) / Ctot), C(k) being the summed weight of warps 0..k-1.
+// skew 0 (or one tier) gives every warp T / Wt pages.
+// floor(a / b) for 0 <= a < 2^53, 0 < b < 2^31: a double-precision quotient, exact up to
+// one unit, then corrected with integer products (cheaper than a 64-bit division).
+__device__ __forceinline__ int64_t floordiv53(int64_t a, int64_t b) {
+  int64_t q = (int64_t)((double)a / (double)b);
+  if (q * b > a) --q;
+  else if ((q + 1) * b <= a) ++q;
+  return q;
+}
+
+// T < 2^31 pages and Ctot <= Wt * 1024 < 2^22, so every product below stays under 2^53.
+struct Shares {
+  int T, Wt;
+  int tier_warps;  // warps per tier
+  int tiers, skew;
+  __device__ __forceinline__ int weight(int t) const { return 1024 - skew * t; }
+  // summed weight of the warps before tier t (t <= tiers)
+  __device__ __forceinline__ int64_t tier_base(int t) const {
+    return (int64_t)tier_warps * (1024 * t - skew * (t * (t - 1) / 2));
+  }
+  __device__ __forceinline__ int64_t cum(int k) const {
+    const int t = min(k / tier_warps, tiers - 1);
+    return tier_base(t) + (int64_t)(k - t * tier_warps) * weight(t);
+  }
+  __device__ __forceinline__ int start(int k) const { return (int)floordiv53((int64_t)T * cum(k), tier_base(tiers)); }
+  // the warp whose share holds flat page f: the largest k with start(k) <= f, i.e.
+  // cum(k) <= X = ceil((f + 1) * Ctot / T) - 1
+  __device__ __forceinline__ int owner(int f) const {
+    const int64_t tot = tier_base(tiers);
+    const int64_t X = floordiv53((int64_t)(f + 1) * tot + T - 1, T) - 1;
+    int t = tiers - 1;
+    while (t > 0 && tier_base(t) > X) --t;
+    const int k = t * tier_warps + (int)((X - tier_base(t)) / weight(t));
+    return min(k, Wt - 1);
+  }
+};
+
+// The shares are divided in a cost space in which every (request, kv head) pair is
+// charged `ovh` virtual pages ahead of its real ones, for the fixed cost of the piece a
+// warp closes on it (partial write, ticket, merge); a share's bounds are then mapped
+// back to real pages.  Request r starts at cost cpre(r) = pre[r] + ovh * Hkv * r.
+struct CostMap {
+  const int* pre;
+  int B, Hkv, ovh;
+  __device__ __forceinline__ int cpre(int r) const { return pre[r] + ovh * Hkv * r; }
+  __device__ __forceinline__ int total() const { return cpre(B); }
+  // real pages before cost position x, 0 <= x <= total()
+  __device__ __forceinline__ int realpos(int x) const {
+    int lo = 0, hi = B;  // the largest r with cpre(r) <= x; its block is never empty unless r == B
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (cpre(mid) <= x) lo = mid; else hi = mid - 1;
+    }
+    if (lo == B) return pre[B];
+    const int nbr = (pre[lo + 1] - pre[lo]) / Hkv, blk = nbr + ovh;
+    const int off = x - cpre(lo), h = off / blk, o = off - h * blk;
+    return pre[lo] + h * nbr + max(0, o - ovh);
+  }
+  // cost position of the first real page of pair (r, h), whose request has nbr pages per head
+  __device__ __forceinline__ int pair_cost(int r, int h, int nbr) const { return cpre(r) + h * (nbr + ovh) + ovh; }
+};
+
+template <int kW>
+__device__ __forceinline__ Shares make_shares(const DecodeParams& p, int T) {
+  const int Wt = (int)gridDim.x * kW;
+  const int tiers = (p.tier_ctas > 0 && (int)gridDim.x % p.tier_ctas == 0) ? (int)gridDim.x / p.tier_ctas : 1;
+  // every tier keeps at least a quarter of the base weight
+  return Shares{T, Wt, Wt / tiers, tiers, tiers > 1 ? min(p.skew, 768 / (tiers - 1)) : 0};
+}
+
+// The last contributor of a (request, kv head) pair merges the partial (O, LSE) slots of
+// warps k0..k1 into the final rows row0 .. row0 + G - 1.  Warp k's slot is 2k, or 2k + 1
+// for k0 when the pair starts inside k0's share (its second piece).  Every partial
+// load is issued without waiting on another: lane j gathers contributor j's LSE together
+// with the first four partial rows, then each lane accumulates head dims 4*lane .. +3
+// four rows at a time.  (Inlined: as an out-of-line call it cost the streaming loop
+// around it 3-5% on B200.)
+__device__ __forceinline__ void merge_pair(const float* part_o, const float* part_lse, __half* out, float* shard_o,
+                                        float* shard_lse, int G, int64_t k0, int64_t k1, bool k0_first,
+                                        size_t row0, int lane) {
+  const int n = (int)(k1 - k0 + 1);
+  auto slot = [&](int j) -> size_t { return ((size_t)(k0 + j) * 2 + ((j == 0 && !k0_first) ? 1 : 0)) * G; };
+  const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int qg = 0; qg < G; ++qg) {
+    auto row = [&](int j) { return __ldcg(reinterpret_cast<const float4*>(part_o + (slot(j) + qg) * kD) + lane); };
+    const float lse_l = lane < n ? __ldcg(part_lse + slot(lane) + qg) : -INFINITY;
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = u < n ? row(u) : zero4;
+    float M = lse_l;
+    for (int j = lane + 32; j < n; j += 32) M = fmaxf(M, __ldcg(part_lse + slot(j) + qg));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float W = 0.f;
+    float4 acc = zero4;
+    if (M != -INFINITY) {
+      for (int j0 = 0; j0 < n; j0 += 32) {
+        const int j = j0 + lane;
+        const float lse = j0 == 0 ? lse_l : (j < n ? __ldcg(part_lse + slot(j) + qg) : -INFINITY);
+        const float w = lse == -INFINITY ? 0.f : expf(lse - M);
+        W += w;
+        const int cnt = min(32, n - j0);
+        for (int q = 0; q < cnt; q += 4) {
+          if (q > 0 || j0 > 0) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = q + u < cnt ? row(j0 + q + u) : zero4;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float wu = __shfl_sync(0xffffffffu, w, (q + u) & 31);
+            acc.x = fmaf(wu, v[u].x, acc.x);
+            acc.y = fmaf(wu, v[u].y, acc.y);
+            acc.z = fmaf(wu, v[u].z, acc.z);
+            acc.w = fmaf(wu, v[u].w, acc.w);
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
+    }
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    const float lse_out = W > 0.f ? M + logf(W) : -INFINITY;
+    const size_t r = row0 + qg;
+    const int d = 4 * lane;
+    if (shard_o != nullptr) {
+      *reinterpret_cast<float4*>(shard_o + r * kD + d) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      if (lane == 0) shard_lse[r] = lse_out;
+    } else {
+      const __half2 h01 = __floats2half2_rn(acc.x * inv, acc.y * inv), h23 = __floats2half2_rn(acc.z * inv, acc.w * inv);
+      uint2 pk;
+      pk.x = *reinterpret_cast<const uint32_t*>(&h01);
+      pk.y = *reinterpret_cast<const uint32_t*>(&h23);
+      *reinterpret_cast<uint2*>(out + r * kD + d) = pk;
+    }
+  }
+}
 
 // largest r with pre[r] <= f (pre ascending, pre[0] = 0, pre[B] = T > f)
 __device__ __forceinline__ int find_request(const int* pre, int B, int f) {
@@ -682,7 +827,17 @@ __device__ __forceinline__ int window_pages(const DecodeParams& p, int r, int lo
   return max(0, min(np, hi_cap) - lo);
 }
 
-template <bool kPaged, int kW, int kNS, int kMaxRegs>
+// Profiling aid: warp w of CTA b stamps %globaltimer into trace[(b * (kW + 1) + w) * 8 + k]:
+// k = 0 kernel entry, 1 after the prologue, 2 first page ready (producer: first issue),
+// 3 last page consumed (producer: last issue), 4 warp done, 5 pages handled, 6 SM id.
+template <bool kTrace>
+__device__ __forceinline__ void trace_mark(const DecodeParams& p, int nwarps, int lane, int k,
+                                           unsigned long long v = 0ull) {
+  if (kTrace && p.trace != nullptr && lane == 0)
+    p.trace[((size_t)blockIdx.x * nwarps + (threadIdx.x >> 5)) * 8 + k] = k >= 5 ? v : globaltimer_ns();
+}
+
+template <bool kPaged, int kW, int kNS, int kMaxRegs, bool kTrace>
 __global__ void __maxnreg__(kMaxRegs)
     decode_balanced_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                            const DecodeParams p) {
@@ -702,8 +857,10 @@ __global__ void __maxnreg__(kMaxRegs)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int B = p.B, Hkv = p.Hkv;
+  int* starts = pre + B + 1;  // [kW + 1]
   const int lo = (int)max(p.page_begin, (int64_t)0);
   const int hi_cap = p.page_end > 0 ? (int)min(p.page_end, (int64_t)0x7fffffff) : 0x7fffffff;
+  trace_mark<kTrace>(p, kW + 1, lane, 0);
 
   if (tid == 0) {
     for (int st = 0; st < kNS; ++st) {
@@ -728,16 +885,22 @@ __global__ void __maxnreg__(kMaxRegs)
       carry += __shfl_sync(0xffffffffu, x, 31);
     }
     if (lane == 0) pre[0] = 0;
+    __syncwarp();
+    // the first flat page of this CTA's warps' shares, and the end of the last one
+    if (lane <= kW) {
+      const CostMap cm{pre, B, Hkv, p.piece_cost};
+      starts[lane] = cm.realpos(make_shares<kW>(p, cm.total()).start((int)blockIdx.x * kW + lane));
+    }
   }
   __syncthreads();
   const int64_t T = pre[B];
-  const int64_t Wt = (int64_t)gridDim.x * kW;
   const float kLn2 = 0.6931471805599453f;
+  trace_mark<kTrace>(p, kW + 1, lane, 1);
 
   if (warp == kW) {
     // ============================ producer warp ===============================
-    constexpr int kIssue = 8;
-    static_assert(kNS % kIssue == 0 && 32 % kIssue == 0 && kIssue % kW == 0, "issue batch must divide the ring");
+    constexpr int kIssue = issue_batch(kNS);
+    static_assert(kNS % kIssue == 0 && 32 % kIssue == 0, "issue batch must divide the ring");
     if (T == 0) return;
     prefetch_tmap(&tmk);
     prefetch_tmap(&tmv);
@@ -748,8 +911,8 @@ __global__ void __maxnreg__(kMaxRegs)
 #pragma unroll
     for (int w = 0; w < kW; ++w) {
       const int64_t k = (int64_t)blockIdx.x * kW + w;
-      sh_start[w] = share_start(k, T, Wt);
-      sh_len[w] = (int)(share_start(k + 1, T, Wt) - sh_start[w]);
+      sh_start[w] = starts[w];
+      sh_len[w] = starts[w + 1] - starts[w];
       max_len = max(max_len, sh_len[w]);
     }
     const int n_issue = max_len * kW;
@@ -786,15 +949,19 @@ __global__ void __maxnreg__(kMaxRegs)
       const long long e = __shfl_sync(0xffffffffu, tcur, (i0 + (lane & (kIssue - 1))) & 31);
       const int i = i0 + lane;
       if (lane < kIssue && e != -2) {
-        const int st = i & (kNS - 1);
-        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (uint32_t)(((i / kNS) - 1) & 1), kProducerSleepNs, kTimeoutNs)) {
+        const int st = (int)((unsigned)i % kNS);
+        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (((unsigned)i / kNS) - 1u) & 1u, kProducerSleepNs, kTimeoutNs)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
         if (!aborted) issue_page(p, &tmk, &tmv, base_s, meta_p, meta_s, full_s + 8 * st, st, e, policy);
       }
+      if (i0 == 0) trace_mark<kTrace>(p, kW + 1, lane, 2);
       if (__any_sync(0xffffffffu, aborted)) break;
     }
+    trace_mark<kTrace>(p, kW + 1, lane, 3);
+    trace_mark<kTrace>(p, kW + 1, lane, 4);
+    trace_mark<kTrace>(p, kW + 1, lane, 5, (unsigned long long)n_issue);
     return;  // the producer takes no part in the epilogue
   }
 
@@ -813,8 +980,8 @@ __global__ void __maxnreg__(kMaxRegs)
   }
   if (T == 0) return;
   const int64_t k = (int64_t)blockIdx.x * kW + warp;
-  const int64_t f_begin = share_start(k, T, Wt);
-  const int len_w = (int)(share_start(k + 1, T, Wt) - f_begin);
+  const int64_t f_begin = starts[warp];
+  const int len_w = starts[warp + 1] - starts[warp];
   const StageOffsets off(lane);
   QueryFrag qf;
   WarpState ws;
@@ -835,11 +1002,12 @@ __global__ void __maxnreg__(kMaxRegs)
       qf.load(p, r, h, lane);
     }
     const int i = j * kW + warp;
-    const int st = i & (kNS - 1);
-    if (!mbar_wait_bounded(full_s + 8 * st, (uint32_t)((i / kNS) & 1), kTimeoutNs)) {
+    const int st = (int)((unsigned)i % kNS);
+    if (!mbar_wait_bounded(full_s + 8 * st, ((unsigned)i / kNS) & 1u, kTimeoutNs)) {
       if (lane == 0 && p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
       return;
     }
+    if (j == 0) trace_mark<kTrace>(p, kW + 1, lane, 2);
     StageInfo si;
     if (read_stage_info(meta_p, st, si)) {
       consume_page<0>(base_s + st * kStageBytes, off, empty_s + 8 * st, lane, si, qf, p.qk_scale_log2,
@@ -848,6 +1016,7 @@ __global__ void __maxnreg__(kMaxRegs)
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_s + 8 * st);
     }
+    if (j + 1 == len_w) trace_mark<kTrace>(p, kW + 1, lane, 3);
     if (f + 1 != pair_end && j + 1 != len_w) continue;
 
     // ---- close the piece ------------------------------------------------------------
@@ -881,63 +1050,41 @@ __global__ void __maxnreg__(kMaxRegs)
 #pragma unroll
       for (int i2 = 0; i2 < 8; ++i2) {
         const int d = 16 * i2 + 2 * g;
-        if (2 * c < p.G) {
-          p.part_o[(slot + 2 * c) * kD + d] = ws.acc[i2][0] * inv0;
-          p.part_o[(slot + 2 * c) * kD + d + 1] = ws.acc[i2][2] * inv0;
-        }
-        if (2 * c + 1 < p.G) {
-          p.part_o[(slot + 2 * c + 1) * kD + d] = ws.acc[i2][1] * inv1;
-          p.part_o[(slot + 2 * c + 1) * kD + d + 1] = ws.acc[i2][3] * inv1;
-        }
+        if (2 * c < p.G)
+          *reinterpret_cast<float2*>(p.part_o + (slot + 2 * c) * kD + d) =
+              make_float2(ws.acc[i2][0] * inv0, ws.acc[i2][2] * inv0);
+        if (2 * c + 1 < p.G)
+          *reinterpret_cast<float2*>(p.part_o + (slot + 2 * c + 1) * kD + d) =
+              make_float2(ws.acc[i2][1] * inv1, ws.acc[i2][3] * inv1);
       }
       const float lq = __shfl_sync(0xffffffffu, l, (4 * lane) & 31);
       const float mq = __shfl_sync(0xffffffffu, ws.m_run, (4 * lane) & 31);
       if (lane < p.G) p.part_lse[slot + lane] = lq > 0.f ? (mq + log2f(lq)) * kLn2 : -INFINITY;
-      const int64_t k0 = share_of(pair_P, T, Wt), k1 = share_of(pair_end - 1, T, Wt);
+      // rebuilt here (T re-read from shared memory) so the loop above keeps no registers for it
+      const CostMap cm{pre, B, Hkv, p.piece_cost};
+      const Shares sh = make_shares<kW>(p, cm.total());
+      const int c0 = cm.pair_cost(r, h, nb);  // cost position of the pair's first page
+      const int64_t k0 = sh.owner(c0), k1 = sh.owner(c0 + nb - 1);
       const unsigned contributors = (unsigned)(k1 - k0 + 1);
       const int pair_id = r * Hkv + h;
-      __threadfence();
+      fence_acq_rel_gpu();  // releases this warp's partial before the ticket
       __syncwarp();
       unsigned ticket = 0;
       if (lane == 0) ticket = atomicAdd(p.counters + pair_id, 1u);
       ticket = __shfl_sync(0xffffffffu, ticket, 0);
       if (ticket == contributors - 1) {  // last contributor: merge the pair
-        __threadfence();
-        const bool k0_first = share_start(k0, T, Wt) == pair_P;
-        for (int qg = 0; qg < p.G; ++qg) {
-          float M = -INFINITY;
-          for (int64_t kk = k0; kk <= k1; ++kk) {
-            const size_t sl = ((size_t)kk * 2 + ((kk == k0 && !k0_first) ? 1 : 0)) * p.G + qg;
-            M = fmaxf(M, __ldcg(p.part_lse + sl));
-          }
-          float W = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-          if (M != -INFINITY) {
-            for (int64_t kk = k0; kk <= k1; ++kk) {
-              const size_t sl = ((size_t)kk * 2 + ((kk == k0 && !k0_first) ? 1 : 0)) * p.G + qg;
-              const float lse = __ldcg(p.part_lse + sl);
-              if (lse == -INFINITY) continue;
-              const float w = expf(lse - M);
-              W += w;
-              const float* src = p.part_o + sl * kD;
-              o0 = fmaf(w, __ldcg(src + lane), o0);
-              o1 = fmaf(w, __ldcg(src + lane + 32), o1);
-              o2 = fmaf(w, __ldcg(src + lane + 64), o2);
-              o3 = fmaf(w, __ldcg(src + lane + 96), o3);
-            }
-          }
-          const float inv = W > 0.f ? 1.f / W : 0.f;
-          const float lse_out = W > 0.f ? M + logf(W) : -INFINITY;
-          write_final(p, row0 + qg, lane, o0 * inv, lse_out);
-          write_final(p, row0 + qg, lane + 32, o1 * inv, lse_out);
-          write_final(p, row0 + qg, lane + 64, o2 * inv, lse_out);
-          write_final(p, row0 + qg, lane + 96, o3 * inv, lse_out);
-        }
+        fence_acq_rel_gpu();
+        merge_pair(p.part_o, p.part_lse, p.out, p.shard_o, p.shard_lse, p.G, k0, k1, sh.start(k0) >= c0 - cm.ovh,
+                   row0, lane);
         if (lane == 0) p.counters[pair_id] = 0u;  // leave the ticket clean for the next call
       }
     }
     first_piece = false;
     ws.reset();
   }
+  trace_mark<kTrace>(p, kW + 1, lane, 4);
+  trace_mark<kTrace>(p, kW + 1, lane, 5, (unsigned long long)len_w);
+  trace_mark<kTrace>(p, kW + 1, lane, 6, (unsigned long long)smid());
 }
 
 // ---------------------------------------------------------------------------------
@@ -951,9 +1098,12 @@ struct Shape {
   int warps, stages, min_blocks, max_regs;  // max_regs: register cap of the balanced kernel
 };
 using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
+// (One CTA per SM with 11-12 consumer warps behind a single producer measured 1.7-2x
+// slower on B200: one slow warp stalls the in-order producer and with it the whole SM.)
 constexpr Shape kShapes[] = {{4, 16, 3, 128}, {8, 16, 2, 112}};
 constexpr int kNumShapes = 2;
-constexpr int kDefaultShape = 0;
+constexpr int kDefaultShape = 0;          // split kernel
+constexpr int kDefaultBalancedShape = 0;  // balanced kernel
 
 template <bool kPaged, int kSi, int kMode>
 __host__ DecodeKernelFn kernel_inst() {
@@ -975,15 +1125,24 @@ static DecodeKernelFn kernel_for(int shape, int mode) {
   return shape == 1 ? kernel_mode<kPaged, 1>(mode) : kernel_mode<kPaged, 0>(mode);
 }
 
-template <bool kPaged, int kSi>
+template <bool kPaged, int kSi, bool kTrace = false>
 __host__ DecodeKernelFn balanced_inst() {
   constexpr Shape sh = kShapes[kSi];
-  return decode_balanced_kernel<kPaged, sh.warps, sh.stages, sh.max_regs>;
+  return decode_balanced_kernel<kPaged, sh.warps, sh.stages, sh.max_regs, kTrace>;
+}
+
+// FLASHSPEC_TRACE_PTR (profiling only): device address of a zeroed uint64 buffer of
+// ctas * (warps + 1) * 8 words; the balanced kernel of shape 0 then records its
+// per-warp timeline there (trace_mark).
+static unsigned long long* trace_ptr() {
+  const char* v = getenv("FLASHSPEC_TRACE_PTR");
+  return v ? reinterpret_cast<unsigned long long*>(strtoull(v, nullptr, 0)) : nullptr;
 }
 
 template <bool kPaged>
 static DecodeKernelFn balanced_for(int shape) {
-  return shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0>();
+  if (shape == 1) return balanced_inst<kPaged, 1>();
+  return trace_ptr() != nullptr ? balanced_inst<kPaged, 0, true>() : balanced_inst<kPaged, 0>();
 }
 
 static int smem_bytes(int shape) {
@@ -992,7 +1151,9 @@ static int smem_bytes(int shape) {
 }
 
 // the balanced kernel adds its per-request prefix table
-static int smem_balanced(int shape, int batch) { return smem_bytes(shape) + ((4 * (batch + 1) + 15) & ~15); }
+static int smem_balanced(int shape, int batch) {
+  return smem_bytes(shape) + ((4 * (batch + 1) + 4 * (kShapes[shape].warps + 1) + 15) & ~15);
+}
 
 // FLASHSPEC_DEBUG_MODE (profiling only, results are wrong when set): 1 = skip the math,
 // 2 = data movement only.
@@ -1012,7 +1173,7 @@ static int shape_choice() {
     for (int s = 0; s < kNumShapes; ++s)
       if (kShapes[s].warps == w) return s;
   }
-  return kDefaultShape;
+  return -1;
 }
 
 template <bool kPaged>
@@ -1020,16 +1181,33 @@ static int configure_kernel(int device, int shape) {
   static bool done[2][kNumShapes][kMaxDevices] = {};
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
-  if (device < 0 || device >= kMaxDevices) return FS_ERR_CUDA;
+  if (device < 0 || device >= kMaxDevices) return fail_cuda("device ordinal beyond the library's table");
   if (done[kPaged][shape][device]) return FS_OK;
+  cudaError_t e;
   for (int mode = 0; mode < 3; ++mode)
-    if (cudaFuncSetAttribute(kernel_for<kPaged>(shape, mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem_bytes(shape)) != cudaSuccess)
-      return FS_ERR_CUDA;
-  if (cudaFuncSetAttribute(balanced_for<kPaged>(shape), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           smem_balanced(shape, kMaxSKBatch)) != cudaSuccess)
-    return FS_ERR_CUDA;
+    if ((e = cudaFuncSetAttribute(kernel_for<kPaged>(shape, mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smem_bytes(shape))) != cudaSuccess)
+      return fail_cuda("shared-memory limit of the split decode kernel", e);
+  const DecodeKernelFn balanced[2] = {shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0>(),
+                                      shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0, true>()};
+  for (DecodeKernelFn fn : balanced)
+    if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_balanced(shape, kMaxSKBatch))) !=
+        cudaSuccess)
+      return fail_cuda("shared-memory limit of the balanced decode kernel", e);
   done[kPaged][shape][device] = true;
+  return FS_OK;
+}
+
+// Raises the shared-memory limits of every kernel a plan may pick (the occupancy queries
+// of the planner need them); the paged instantiations are the ones those queries use.
+template <bool kPaged>
+static int configure_shapes(int device, int forced) {
+  const int shapes[2] = {forced >= 0 ? forced : kDefaultShape, forced >= 0 ? forced : kDefaultBalancedShape};
+  for (int sh : shapes) {
+    int st = configure_kernel<kPaged>(device, sh);
+    if (st == FS_OK) st = configure_kernel<true>(device, sh);
+    if (st != FS_OK) return st;
+  }
   return FS_OK;
 }
 
@@ -1070,7 +1248,7 @@ static EncodeTiledFn encode_fn() {
 // landing in shared memory with the 128-byte swizzle.
 static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
   EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr) return FS_ERR_CUDA;
+  if (enc == nullptr) return fail_cuda("cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kD};
   cuuint32_t box[2] = {(cuuint32_t)kD, (cuuint32_t)kPage};
@@ -1078,7 +1256,7 @@ static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? FS_OK : FS_ERR_CUDA;
+  return r == CUDA_SUCCESS ? FS_OK : fail_cuda("cuTensorMapEncodeTiled", r);
 }
 
 static int64_t max_pages_of(const FsDecodeArgs* a) {
@@ -1133,6 +1311,7 @@ struct Plan {
   bool balanced;
   int splits;
   int ctas;
+  int shape;
 };
 
 static int balanced_per_sm(int device, int shape, int batch) {
@@ -1154,6 +1333,28 @@ static int balanced_per_sm(int device, int shape, int batch) {
   return c;
 }
 
+// Weight step between CTA tiers of the balanced kernel, in 1/1024 (Shares).
+// FLASHSPEC_TIER_SKEW overrides it (profiling).
+static int tier_skew() {
+  constexpr int kDefaultSkew = 26;  // B200 sweep of the benchmark configurations
+  if (const char* v = getenv("FLASHSPEC_TIER_SKEW")) {
+    const int s = atoi(v);
+    if (s >= 0 && s <= 256) return s;
+  }
+  return kDefaultSkew;
+}
+
+// Virtual pages the balanced kernel charges per (request, kv head) pair (CostMap).
+// FLASHSPEC_PIECE_COST overrides it (profiling).
+constexpr int kDefaultPieceCost = 6;  // B200 sweep of the benchmark configurations
+static int piece_cost() {
+  if (const char* v = getenv("FLASHSPEC_PIECE_COST")) {
+    const int c = atoi(v);
+    if (c >= 0 && c <= 64) return c;
+  }
+  return kDefaultPieceCost;
+}
+
 // FLASHSPEC_DECODE_KERNEL=split|balanced forces a kernel (profiling, tests).
 static int kernel_override() {
   const char* v = getenv("FLASHSPEC_DECODE_KERNEL");
@@ -1166,20 +1367,26 @@ static int kernel_override() {
 // An explicit num_splits selects the split kernel.  Otherwise the balanced kernel runs
 // when there are more (request, kv head) pairs than resident CTAs (then split CTAs come
 // in several unequal waves); with fewer pairs the split kernel fills exactly one wave.
-static Plan make_plan(const FsDecodeArgs* a, int device, int shape) {
-  Plan pl{false, 1, 0};
+// `forced` is a shape from FLASHSPEC_KERNEL_SHAPE / FLASHSPEC_NUM_WARPS or -1; each kernel
+// otherwise runs its own default shape.
+static Plan make_plan(const FsDecodeArgs* a, int device, int forced) {
+  Plan pl{false, 1, 0, 0};
   const int ov = kernel_override();
   const int64_t pairs = (int64_t)a->batch * a->kv_heads;
   const int64_t maxp = max_pages_of(a);
+  const int shape = forced >= 0 ? forced : kDefaultBalancedShape;
+  const int split_shape = forced >= 0 ? forced : kDefaultShape;
   const int warps = kShapes[shape].warps;
-  bool balanced = a->num_splits <= 0 && a->batch <= kMaxSKBatch && maxp > 0 && pairs * maxp < (1ll << 31);
+  bool balanced = a->num_splits <= 0 && a->batch <= kMaxSKBatch && maxp > 0 && pairs * (maxp + 64) < (1ll << 31);
   if (balanced) {
     const int64_t slots = (int64_t)balanced_per_sm(device, shape, a->batch) * device_sm_count(device);
     const int64_t t_est = pairs * maxp;
     pl.ctas = (int)std::max<int64_t>(1, std::min<int64_t>(slots, t_est / (warps * 4)));
+    // the share arithmetic (Shares) needs fewer than 4096 warps
+    pl.ctas = (int)std::min<int64_t>(pl.ctas, 4095 / warps);
     // With no more pairs than resident CTAs the split kernel already fills one wave with
     // equal CTAs (measured faster); with few long pairs the merges would serialise.
-    const int64_t split_slots = resident_ctas(device, shape);
+    const int64_t split_slots = resident_ctas(device, split_shape);
     const int64_t contributors = (int64_t)pl.ctas * warps / pairs + 1;
     if ((contributors > 16 || pairs <= split_slots) && ov != 2) balanced = false;
     if (ov == 1) balanced = false;
@@ -1187,8 +1394,10 @@ static Plan make_plan(const FsDecodeArgs* a, int device, int shape) {
   if (balanced) {
     pl.balanced = true;
     pl.splits = 0;
+    pl.shape = shape;
   } else {
-    pl.splits = resolve_splits(a, device, shape);
+    pl.splits = resolve_splits(a, device, split_shape);
+    pl.shape = split_shape;
   }
   return pl;
 }
@@ -1241,11 +1450,11 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   int st = validate(a, kPaged ? FS_LAYOUT_PAGED : FS_LAYOUT_CONTIGUOUS);
   if (st != FS_OK) return st;
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
-  const int shape = shape_choice();
-  if ((st = configure_kernel<kPaged>(device, shape)) != FS_OK) return st;
-  if ((st = configure_kernel<true>(device, shape)) != FS_OK) return st;
-  const Plan pl = make_plan(a, device, shape);
+  if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+  const int forced = shape_choice();
+  if ((st = configure_shapes<kPaged>(device, forced)) != FS_OK) return st;
+  const Plan pl = make_plan(a, device, forced);
+  const int shape = pl.shape;
   const size_t need = pl.balanced ? workspace_balanced(a, pl.ctas, shape) : workspace_for(a, pl.splits);
   if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need)) return FS_ERR_WORKSPACE;
   if ((pl.balanced || pl.splits > 1) && (a->tickets == nullptr || a->ticket_count < (int64_t)a->batch * a->kv_heads))
@@ -1269,6 +1478,7 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.shard_o = a->shard_o;
   p.shard_lse = a->shard_lse;
   p.status = a->device_status;
+  p.trace = trace_ptr();
   p.B = a->batch;
   p.Hq = a->q_heads;
   p.Hkv = a->kv_heads;
@@ -1281,6 +1491,9 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.page_end = a->page_end;
   p.zp_count = kPaged ? a->num_blocks * a->kv_heads : (int64_t)a->batch * a->kv_heads * a->num_blocks;
   p.qk_scale_log2 = a->sm_scale * 1.4426950408889634f;
+  p.tier_ctas = device_sm_count(device);
+  p.skew = tier_skew();
+  p.piece_cost = piece_cost();
   if (need > 0) {
     const size_t G = (size_t)p.G;
     const size_t units = pl.balanced ? (size_t)pl.ctas * kShapes[shape].warps * 2 * G
@@ -1300,7 +1513,7 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
     kernel_for<kPaged>(shape, debug_mode())<<<(unsigned)grid, threads, smem_bytes(shape),
                                               reinterpret_cast<cudaStream_t>(stream)>>>(tmk, tmv, p);
   }
-  return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
+  return launch_status(pl.balanced ? "balanced decode kernel launch" : "split decode kernel launch");
 }
 
 }  // namespace fsb
@@ -1312,11 +1525,11 @@ int fs_decode_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* spli
   int st = fsb::validate(a, a->layout);
   if (st != FS_OK) return st;
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
-  const int shape = fsb::shape_choice();
-  if ((st = fsb::configure_kernel<true>(device, shape)) != FS_OK) return st;
-  const fsb::Plan pl = fsb::make_plan(a, device, shape);
-  *bytes = pl.balanced ? fsb::workspace_balanced(a, pl.ctas, shape) : fsb::workspace_for(a, pl.splits);
+  if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fsb::fail_cuda("cudaGetDevice", e);
+  const int forced = fsb::shape_choice();
+  if ((st = fsb::configure_shapes<true>(device, forced)) != FS_OK) return st;
+  const fsb::Plan pl = fsb::make_plan(a, device, forced);
+  *bytes = pl.balanced ? fsb::workspace_balanced(a, pl.ctas, pl.shape) : fsb::workspace_for(a, pl.splits);
   if (splits_out) *splits_out = pl.balanced ? 0 : pl.splits;
   return FS_OK;
 }

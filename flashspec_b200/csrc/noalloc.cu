@@ -50,11 +50,12 @@ static size_t partial_bytes(const FsDecodeArgs* a, int64_t splits) {
 static int scratch_address(int device, unsigned char** out) {
   static unsigned char* addr[kMaxDevices] = {};
   static std::mutex mu;
-  if (device < 0 || device >= kMaxDevices) return FS_ERR_CUDA;
+  if (device < 0 || device >= kMaxDevices) return fail_cuda("device ordinal beyond the library's table");
   std::lock_guard<std::mutex> lock(mu);
   if (addr[device] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return FS_ERR_CUDA;
+    if (cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch); e != cudaSuccess || p == nullptr)
+      return fail_cuda("cudaGetSymbolAddress of the no-alloc scratch", e);
     addr[device] = static_cast<unsigned char*>(p);
   }
   *out = addr[device];
@@ -81,16 +82,17 @@ extern "C" int fs_paged_decode_noalloc(const FsDecodeArgs* args, void* stream) {
   a.num_splits = splits;  // the launch below must use the split count checked here
 
   int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return FS_ERR_CUDA;
+  if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
   unsigned char* scratch = nullptr;
   if ((st = scratch_address(device, &scratch)) != FS_OK) return st;
   a.tickets = reinterpret_cast<uint32_t*>(scratch);
   a.ticket_count = (int64_t)(kTicketBytes / 4);
   a.workspace = scratch + kTicketBytes;
   a.workspace_bytes = kPartialBytes;
-  if (splits > 1 &&
-      cudaMemsetAsync(a.tickets, 0, (size_t)a.batch * a.kv_heads * 4, reinterpret_cast<cudaStream_t>(stream)) !=
-          cudaSuccess)
-    return FS_ERR_CUDA;
+  if (splits > 1) {
+    const cudaError_t e =
+        cudaMemsetAsync(a.tickets, 0, (size_t)a.batch * a.kv_heads * 4, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail_cuda("cudaMemsetAsync of the no-alloc tickets", e);
+  }
   return fs_paged_decode(&a, stream);
 }

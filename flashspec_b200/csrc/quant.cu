@@ -15,6 +15,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include "common.h"
+
 #include "../../include/flashspec_b200.h"
 
 namespace fsb {
@@ -207,6 +209,8 @@ const char* fs_status_string(int s) {
   }
 }
 
+const char* fs_last_error_detail(void) { return fsb::g_error_detail; }
+
 int fs_quantize_blocks(const FsQuantizeArgs* a, void* stream) {
   if (a == nullptr || a->x == nullptr || a->values == nullptr || a->scale == nullptr || a->zero_point == nullptr)
     return FS_ERR_INVALID_ARGUMENT;
@@ -217,7 +221,7 @@ int fs_quantize_blocks(const FsQuantizeArgs* a, void* stream) {
   if (grid >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
   fsb::quantize_blocks_kernel<<<(unsigned)grid, fsb::kQThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       a->x, a->x_dtype, a->seq_len, a->head_dim, a->block_size, nblk, a->values, a->scale, a->zero_point);
-  return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
+  return fsb::launch_status("quantize kernel launch");
 }
 
 int fs_page_update(const FsPageUpdateArgs* a, void* stream) {
@@ -232,7 +236,7 @@ int fs_page_update(const FsPageUpdateArgs* a, void* stream) {
   if (a->heads > 65535) return FS_ERR_UNSUPPORTED;
   dim3 grid((unsigned)a->n_items, (unsigned)a->heads);
   fsb::page_update_kernel<<<grid, fsb::kUThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a->items, *a);
-  return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
+  return fsb::launch_status("page update kernel launch");
 }
 
 int fs_dequantize_pages(const int8_t* values, const float* scale, const int16_t* zero_point, const int64_t* pages,
@@ -246,7 +250,7 @@ int fs_dequantize_pages(const int8_t* values, const float* scale, const int16_t*
   dim3 grid((unsigned)n_listed, (unsigned)heads);
   fsb::dequantize_pages_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       values, scale, zero_point, pages, num_pages, heads, block_size, head_dim, out);
-  return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
+  return fsb::launch_status("dequantize kernel launch");
 }
 
 int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows, int32_t head_dim,
@@ -260,7 +264,7 @@ int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_pa
   if (blocks >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
   fsb::merge_partials_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       o_parts, lse_parts, n_parts, rows, head_dim, part_stride < 0 ? 0 : part_stride, out, out_dtype);
-  return cudaGetLastError() == cudaSuccess ? FS_OK : FS_ERR_CUDA;
+  return fsb::launch_status("merge kernel launch");
 }
 
 }  // extern "C"

@@ -86,6 +86,10 @@ typedef struct FsDecodeArgs {
 /* Library version / ABI check. */
 int fs_abi_version(void);
 const char* fs_status_string(int status);
+/* After a call returned FS_ERR_CUDA: which CUDA call failed and its error, for this
+ * thread (empty before the first such failure).  No reference counterpart: the
+ * reference surfaces CUDA errors as Python exceptions from its launcher. */
+const char* fs_last_error_detail(void);
 
 /* Bytes of workspace a call with these arguments needs (0 when num_splits
  * resolves to 1; the call then needs batch*kv_heads zeroed tickets as well).  Resolves num_splits==0 with the library policy and reports

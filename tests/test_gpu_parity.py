@@ -385,6 +385,28 @@ def test_balanced_kernel_deterministic_and_matches_split(monkeypatch):
     close(a, c.float().cpu().numpy(), atol=1e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("skew,cost", [(0, 0), (256, 0), (0, 64), (200, 17)])
+def test_balanced_share_division_variants(monkeypatch, skew, cost):
+    """Tier weights and per-pair piece costs only move the share boundaries of the
+    balanced kernel: any setting gives the oracle's result.  The batch is large enough
+    for a full grid (three CTA tiers per SM) and mixes empty requests, one-token requests
+    and pairs shorter than a share."""
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "balanced")
+    monkeypatch.setenv("FLASHSPEC_TIER_SKEW", str(skew))
+    monkeypatch.setenv("FLASHSPEC_PIECE_COST", str(cost))
+    lens = [3000, 0, 1, 17, 450, 0, 2049, 96, 5, 1200] * 3
+    rng = np.random.default_rng(skew + cost)
+    q, oc = _random_paged(rng, len(lens), 16, 8, [max(n, 1) for n in lens])
+    oc.lengths[:] = lens
+    out = fs().paged_quant_attention_cuda(dev(q), _cache_dev(oc))
+    ref = O.paged_quant_attention(q, oc)
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.all(out[i] == 0)
+        else:
+            close(out[i], ref[i])
+
+
 def test_balanced_page_windows_merge_equal_full(monkeypatch):
     monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "balanced")
     rng = np.random.default_rng(8)
