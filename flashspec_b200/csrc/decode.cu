@@ -1098,8 +1098,9 @@ struct Shape {
   int warps, stages, min_blocks, max_regs;  // max_regs: register cap of the balanced kernel
 };
 using DecodeKernelFn = void (*)(CUtensorMap, CUtensorMap, DecodeParams);
-// (One CTA per SM with 11-12 consumer warps behind a single producer measured 1.7-2x
-// slower on B200: one slow warp stalls the in-order producer and with it the whole SM.)
+// Measured alternatives on B200 (cfg1): one CTA per SM with 11-12 consumer warps behind a
+// single producer, 1.7-2x slower (one slow warp stalls the in-order producer and with it
+// the whole SM); 2 CTAs of 6 consumer warps, 10% slower; 4 CTAs of 3, no faster.
 constexpr Shape kShapes[] = {{4, 16, 3, 128}, {8, 16, 2, 112}};
 constexpr int kNumShapes = 2;
 constexpr int kDefaultShape = 0;          // split kernel
@@ -1137,6 +1138,11 @@ __host__ DecodeKernelFn balanced_inst() {
 static unsigned long long* trace_ptr() {
   const char* v = getenv("FLASHSPEC_TRACE_PTR");
   return v ? reinterpret_cast<unsigned long long*>(strtoull(v, nullptr, 0)) : nullptr;
+}
+
+template <bool kPaged>
+static DecodeKernelFn balanced_for_untraced(int shape) {
+  return shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0>();
 }
 
 template <bool kPaged>
@@ -1188,8 +1194,8 @@ static int configure_kernel(int device, int shape) {
     if ((e = cudaFuncSetAttribute(kernel_for<kPaged>(shape, mode), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   smem_bytes(shape))) != cudaSuccess)
       return fail_cuda("shared-memory limit of the split decode kernel", e);
-  const DecodeKernelFn balanced[2] = {shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0>(),
-                                      shape == 1 ? balanced_inst<kPaged, 1>() : balanced_inst<kPaged, 0, true>()};
+  const DecodeKernelFn balanced[2] = {balanced_for_untraced<kPaged>(shape),
+                                      shape == 0 ? balanced_inst<kPaged, 0, true>() : balanced_for_untraced<kPaged>(shape)};
   for (DecodeKernelFn fn : balanced)
     if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_balanced(shape, kMaxSKBatch))) !=
         cudaSuccess)
