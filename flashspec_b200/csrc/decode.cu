@@ -616,18 +616,45 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     }
     __syncthreads();
   }
-  for (int idx = tid; idx < nout; idx += kThreads) {
+  if (fits) {
+    // every split wrote its partial row (an empty one with weight 0), so each thread
+    // streams 4 head dims of a query over all splits, eight 16-byte loads in flight
+    constexpr int kBatch = 8;
+    const size_t stride = (size_t)p.G * kD;  // floats between splits
+    for (int u4 = tid; u4 < nout / 4; u4 += kThreads) {
+      const int qg = (4 * u4) >> 7;
+      const int d = (4 * u4) & (kD - 1);
+      const float* src = p.part_o + ((size_t)bh * S * p.G + qg) * kD + d;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s0 = 0; s0 < S; s0 += kBatch) {
+        float4 v[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+          v[u] = s0 + u < S ? __ldcg(reinterpret_cast<const float4*>(src + (size_t)(s0 + u) * stride))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+          const float w = s0 + u < S ? wsm[(s0 + u) * p.G + qg] : 0.f;
+          o.x = fmaf(w, v[u].x, o.x);
+          o.y = fmaf(w, v[u].y, o.y);
+          o.z = fmaf(w, v[u].z, o.z);
+          o.w = fmaf(w, v[u].w, o.w);
+        }
+      }
+      const float lse_out = wsm[nw + qg];
+      const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
+      write_final(p, row, d, o.x, lse_out);
+      write_final(p, row, d + 1, o.y, lse_out);
+      write_final(p, row, d + 2, o.z, lse_out);
+      write_final(p, row, d + 3, o.w, lse_out);
+    }
+  }
+  for (int idx = fits ? nout : tid; idx < nout; idx += kThreads) {
     const int qg = idx >> 7;
     const int d = idx & (kD - 1);
     const size_t prow0 = (size_t)bh * S * p.G + qg;
     float o = 0.f, lse_out;
-    if (fits) {
-      for (int s2 = 0; s2 < S; ++s2) {
-        const float w = wsm[s2 * p.G + qg];
-        if (w != 0.f) o = fmaf(w, __ldcg(p.part_o + (prow0 + (size_t)s2 * p.G) * kD + d), o);
-      }
-      lse_out = wsm[nw + qg];
-    } else {
+    {
       float M = -INFINITY;
       for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(p.part_lse + prow0 + (size_t)s2 * p.G));
       float W = 0.f, O = 0.f;
