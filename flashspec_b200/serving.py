@@ -97,6 +97,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
     tokens = finished = admitted = 0
     ev = lambda: torch.cuda.Event(enable_timing=True)
     step_times = []
+    marks = []
     wall0 = time.perf_counter()
     for step in range(cfg.steps):
         s0 = ev()
@@ -161,13 +162,14 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
                 finished += 1
         s1 = ev()
         s1.record()
-        if measure:
-            s1.synchronize()
-            t_attn += t0.elapsed_time(t1)
-            t_append += a0.elapsed_time(a1)
-            t_prefill += p0.elapsed_time(p1)
-            step_times.append(s0.elapsed_time(s1))
+        if measure:  # read after the loop: no host synchronisation inside it
+            marks.append((s0, s1, p0, p1, a0, a1, t0, t1))
     torch.cuda.synchronize(device)
+    for s0, s1, p0, p1, a0, a1, t0, t1 in marks:
+        t_attn += t0.elapsed_time(t1)
+        t_append += a0.elapsed_time(a1)
+        t_prefill += p0.elapsed_time(p1)
+        step_times.append(s0.elapsed_time(s1))
     wall = time.perf_counter() - wall0
     if recorder is not None:
         recorder.append(("final", alloc, None, None))
