@@ -72,3 +72,26 @@ def test_cuda_entry_points_refuse_cpu_tensors():
 
     with pytest.raises(RuntimeError):
         f.quantize_int8_per_block(torch.zeros(2, 16, 8))
+
+
+def test_cuda_failure_reports_the_failing_call():
+    """A valid decode description queried without a usable GPU fails with FS_ERR_CUDA,
+    and fs_last_error_detail names the CUDA call and its error; with a GPU the query
+    succeeds and the detail is not consulted."""
+    from flashspec_b200 import _lib
+
+    lib = _lib.load()
+    a = _lib.FsDecodeArgs()
+    a.layout = _lib.FS_LAYOUT_PAGED
+    a.q = a.k_values = a.v_values = a.k_scale = a.v_scale = a.k_zero = a.v_zero = 4096
+    a.block_table = a.lengths = a.out = 4096
+    a.batch, a.q_heads, a.kv_heads, a.head_dim, a.block_size = 2, 8, 8, 128, 16
+    a.num_blocks, a.table_cols, a.max_seq_len = 64, 4, 64
+    a.sm_scale = 128 ** -0.5
+    n, s = C.c_size_t(0), C.c_int32(0)
+    st = lib.fs_decode_workspace_size(C.byref(a), C.byref(n), C.byref(s))
+    if st == 0:
+        pytest.skip("a GPU is usable here: no CUDA failure to report")
+    assert st == 3  # FS_ERR_CUDA
+    detail = lib.fs_last_error_detail().decode()
+    assert "cuda" in detail.lower() and ":" in detail, detail
