@@ -7,28 +7,24 @@
 // masked softmax over min(len, max_seq_len) tokens, out = softmax . dequant(v),
 // fp32 accumulation, fp16 output, empty sequences -> 0 (triton_utils.py:181-186).
 //
-// Design (one CTA = one (request, kv head, split) work item, 4 warps):
-//  * A (page, head) block is 16 tokens x 128 B of K plus the same of V, contiguous in
-//    HBM.  Each warp owns a private ring of kStages stages; one lane issues two 2-D
-//    TMA tile loads (K and V, 128B-swizzled into shared memory) and 4-byte cp.async
-//    copies of the page's scale / zero-point words, all completing on one mbarrier.
-//    Pages of the CTA's range are dealt round-robin to the warps; block_table
-//    entries for the next 64 pages are held in registers and broadcast by shuffle.
-//  * Dequantization is fused into the MMA operands: a byte u (uint8 domain) becomes
-//    the exact fp16 value 1024+u by a byte permute against 0x64 exponent bytes,
-//    and one f16x2 subtract of (1024+zp) gives the exact integer u-zp.  The page
-//    scale is applied to fp32 scores (K) and folded into the fp16 probabilities (V).
-//  * QK^T and PV run on the tensor cores (mma.sync m16n8k16, fp16 in, fp32
-//    accumulate).  QK: M = query heads of the GQA group (<= 8 rows used), N = 8
-//    tokens, K = head_dim; PV: M = head_dim, N = query heads, K = the 16 tokens
-//    of a page.  The S accumulator layout is exactly the PV B-operand layout, so
-//    probabilities never leave registers.  The reduction orders over head_dim and
-//    over tokens are permuted so that every thread reads 16-byte vectors.
-//  * Online softmax in the log2 domain with fp32 (m, l) per query; rescaling only
-//    when some row max grows.  Warps are merged through shared memory at the end.
-//  * Split-K: each split writes (O, LSE) to the workspace; the last CTA of a
-//    (request, kv head) -- found with an atomic ticket -- merges them and writes
-//    the fp16 output (or, in shard mode, the merged (O, LSE) partial).
+// Design.  A CTA is 4 consumer warps plus 1 producer warp; 3 CTAs per SM.
+//  * A (page, kv head) block is 16 tokens x 128 B of K plus the same of V, contiguous
+//    in HBM.  The producer keeps a ring of 16 stages full: 8 lanes issue 8 pages per
+//    warp instruction, each two 2-D TMA tile loads (128B-swizzled into shared memory)
+//    and 4-byte cp.async copies of the page's scale / zero-point words, completing on
+//    the stage's full mbarrier.  Page i goes to consumer warp i % 4, stage i % 16.
+//  * QK^T runs on the int8 tensor cores straight from the stored bytes (q held as
+//    16-bit fixed point split into two signed bytes, mma.sync m16n8k32 s8); the zero
+//    point is applied per page with the exact integer sum of q.  PV runs on fp16
+//    tensor cores: a V byte becomes the exact fp16 1024+u (XOR + byte permute against
+//    0x64 exponent bytes) and the zero point is subtracted once per piece from a
+//    per-row sum of the fp16 probabilities.  The page's V scale is folded into them.
+//  * Online softmax in the log2 domain with fp32 (m, l) per query; rescaling only when
+//    a row max grows.
+//  * Two ways to deal pages: decode_kernel (one CTA per (request, kv head, split); the
+//    last CTA of a pair merges the splits' (O, LSE)) and decode_balanced_kernel (a
+//    persistent grid, contiguous per-warp shares of all pages, the last contributor of
+//    a pair merging its pieces).  The host plan picks one per call.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
