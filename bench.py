@@ -268,8 +268,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
         decoder = SequenceShardedDecoder()
         n_pages = cache.block_table.shape[1]
-        if world == 1:
-            replay, _ = decoder.capture(q, cache, n_pages)  # one CUDA graph per step
+        # one CUDA graph per step, unless the step holds an NCCL collective
+        graphable = world == 1 or decoder.transport == "p2p"
+        if graphable:
+            replay, _ = decoder.capture(q, cache, n_pages)
 
             def call():
                 replay()
@@ -346,7 +348,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         q_dev, table_dev, lengths_dev = torch.empty_like(q), torch.empty_like(cache.block_table), torch.empty_like(cache.lengths)
         cache_e2e = fs.PagedKVCache(cache.k_quant, cache.v_quant, table_dev, lengths_dev, cache.block_size,
                                     cache.max_seq_len)
-        if world == 1:
+        if graphable:
             q_dev.copy_(q)
             table_dev.copy_(cache.block_table)
             lengths_dev.copy_(cache.lengths)
@@ -356,7 +358,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             q_dev.copy_(q_host, non_blocking=True)
             table_dev.copy_(table_host, non_blocking=True)
             lengths_dev.copy_(lengths_host, non_blocking=True)
-            if world == 1:
+            if graphable:
                 replay_e2e()
                 out = out_e2e
             else:
@@ -454,7 +456,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "vs_baseline": None, "dtype": "int8 KV, fp16 q/out, fp32 accumulate", "data": "synthetic",
         "config": {"workload": wl.name, "global_batch": len(wl.lengths) * (1 if seqshard else world),
                    "seq_len": max(wl.lengths), "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "page": 16,
-                   "parallelism": (f"sequence-shard x{world} (NCCL all-gather of O/LSE + merge)" if seqshard
+                   "parallelism": (f"sequence-shard x{world} ({'peer-memory exchange' if decoder.transport == 'p2p' else 'NCCL all-gather'} of O/LSE + merge)" if seqshard
                                    else f"request-shard x{world}" if world > 1 else "single"),
                    "l2": "inputs larger than L2 (no flush)", "bytes_per_call_per_gpu": wl.bytes_per_call},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",

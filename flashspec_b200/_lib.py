@@ -112,6 +112,27 @@ class FsPageUpdateArgs(C.Structure):
     ]
 
 
+EXCHANGE_MAX_RANKS = 8
+EXCHANGE_HANDLE_BYTES = 64
+
+
+class FsExchangeArgs(C.Structure):
+    _fields_ = [
+        ("world", C.c_int32),
+        ("rank", C.c_int32),
+        ("bufs", C.c_void_p * EXCHANGE_MAX_RANKS),
+        ("slot_floats", C.c_int64),
+        ("o_mine", C.c_void_p),
+        ("lse_mine", C.c_void_p),
+        ("rows", C.c_int64),
+        ("head_dim", C.c_int32),
+        ("out", C.c_void_p),
+        ("out_dtype", C.c_int32),
+        ("timeout_ns", C.c_int64),
+        ("device_status", C.c_void_p),
+    ]
+
+
 # every symbol the header declares, with its signature
 SIGNATURES = {
     "fs_abi_version": (C.c_int, []),
@@ -124,6 +145,11 @@ SIGNATURES = {
     "fs_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int64, C.c_void_p,
                                     C.c_int32, C.c_void_p]),
     "fs_quantize_blocks": (C.c_int, [C.POINTER(FsQuantizeArgs), C.c_void_p]),
+    "fs_exchange_create": (C.c_int, [C.c_int64, C.POINTER(C.c_void_p), C.c_void_p]),
+    "fs_exchange_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "fs_exchange_close": (C.c_int, [C.c_void_p]),
+    "fs_exchange_destroy": (C.c_int, [C.c_void_p]),
+    "fs_exchange_merge": (C.c_int, [C.POINTER(FsExchangeArgs), C.c_void_p]),
     "fs_page_update": (C.c_int, [C.POINTER(FsPageUpdateArgs), C.c_void_p]),
     "fs_dequantize_pages": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                       C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),

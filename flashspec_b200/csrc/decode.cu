@@ -933,7 +933,6 @@ __global__ void __maxnreg__(kMaxRegs)
     int max_len = 0;
 #pragma unroll
     for (int w = 0; w < kW; ++w) {
-      const int64_t k = (int64_t)blockIdx.x * kW + w;
       sh_start[w] = starts[w];
       sh_len[w] = starts[w + 1] - starts[w];
       max_len = max(max_len, sh_len[w]);

@@ -7,13 +7,16 @@ Two strategies (the reference has no multi-GPU path; SURVEY of the hot path):
 * sequence sharding of long requests (config 3): rank r owns the contiguous logical
   pages ``page_window(n_pages, r, N)`` of every request and only those pages are
   resident on it.  Each rank computes a normalised partial (O fp32, LSE fp32) over
-  its window with the page-window mode of the decode kernel, the partials are
-  all-gathered (NCCL over NVLink; 2*B*Hq*(D+1)*4 bytes per rank) and merged with the
-  log-sum-exp rule of ``fs_merge_partials`` -- the same math as the split-K combine
-  (src/flashspec/triton_fused.py:446-503) applied across GPUs.
+  its window with the page-window mode of the decode kernel; one exchange kernel
+  (``fs_exchange_merge``) stores the rank's rows into every rank's exchange buffer over
+  NVLink and merges all ranks' rows with the log-sum-exp rule -- the same math as the
+  split-K combine (src/flashspec/triton_fused.py:446-503) applied across GPUs.  The
+  NCCL all-gather + ``fs_merge_partials`` step remains as ``transport="nccl"``.
 """
 
 from __future__ import annotations
+
+import os
 
 from typing import Callable, List, Optional, Sequence, Tuple
 
@@ -56,25 +59,106 @@ def _cuda_merge(o_parts, lse_parts, out_dtype):
     return merge_partials(o_parts, lse_parts, out_dtype)
 
 
+class PeerExchange:
+    """The exchange buffers of one group of ranks (one process per GPU of a node): this
+    rank's own, created by the library, and every peer's, mapped through its CUDA IPC
+    handle (handles travel once through ``torch.distributed.all_gather_object``).
+    ``merge`` runs ``fs_exchange_merge``: this rank's partial rows go to every rank over
+    NVLink and the merged rows come back in ``out``, with no collective-library call."""
+
+    def __init__(self, group, device: torch.device, slot_floats: int, timeout_ns: int):
+        import ctypes as C
+
+        from . import _lib
+
+        self._lib = _lib.load()
+        self.device = device
+        self.slot_floats = slot_floats
+        self.timeout_ns = timeout_ns
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > _lib.EXCHANGE_MAX_RANKS:
+            raise ValueError(f"the peer exchange serves at most {_lib.EXCHANGE_MAX_RANKS} ranks")
+        own = C.c_void_p()
+        handle = (C.c_char * _lib.EXCHANGE_HANDLE_BYTES)()
+        with torch.cuda.device(device):
+            _lib.check(self._lib.fs_exchange_create(slot_floats, C.byref(own), handle), "fs_exchange_create")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._peers = []
+        bufs = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bufs.append(self._own)
+                    continue
+                hb = (C.c_char * _lib.EXCHANGE_HANDLE_BYTES).from_buffer_copy(h)
+                p = C.c_void_p()
+                _lib.check(self._lib.fs_exchange_open(hb, C.byref(p)), "fs_exchange_open")
+                self._peers.append(p.value)
+                bufs.append(p.value)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._args = _lib.FsExchangeArgs()
+        self._args.world, self._args.rank = self.world, self.rank
+        for r, b in enumerate(bufs):
+            self._args.bufs[r] = b
+        self._args.slot_floats = slot_floats
+        self._args.timeout_ns = timeout_ns
+        self._args.device_status = self.status.data_ptr()
+
+    def merge(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        import ctypes as C
+
+        from . import _lib
+        from .quant import stream_of
+
+        a = self._args
+        a.o_mine, a.lse_mine = o.data_ptr(), lse.data_ptr()
+        a.rows, a.head_dim = lse.numel(), o.shape[-1]
+        a.out = out.data_ptr()
+        a.out_dtype = {torch.float16: _lib.FS_F16, torch.float32: _lib.FS_F32}[out.dtype]
+        _lib.check(self._lib.fs_exchange_merge(C.byref(a), stream_of(self.device)), "fs_exchange_merge")
+        return out
+
+    def close(self) -> None:
+        with torch.cuda.device(self.device):
+            for p in self._peers:
+                self._lib.fs_exchange_close(p)
+            self._peers = []
+            if self._own:
+                self._lib.fs_exchange_destroy(self._own)
+                self._own = None
+
+
 class SequenceShardedDecoder:
     """Decode one batch whose KV pages are split across the ranks of ``group``.
 
-    Default (CUDA) path per call: the rank's partial (O, LSE) is written by the decode
-    kernel straight into its slot of a preallocated [world, O | LSE] fp32 buffer, one
-    in-place ``all_gather_into_tensor`` fills the other slots (NCCL over NVLink), and
-    ``fs_merge_partials`` merges the strided slots into the fp16 output.  ``capture``
-    records that whole step as a CUDA graph so a step costs one graph replay.
+    Default (CUDA) path per call: the decode kernel writes the rank's partial (O, LSE)
+    into a preallocated [O | LSE] fp32 buffer; with more than one rank the peer-memory
+    exchange (``PeerExchange``, transport "p2p") delivers every rank's rows to every rank
+    and merges them into the fp16 output in one kernel, or (transport "nccl", also
+    ``FLASHSPEC_EXCHANGE=nccl``) an out-of-place ``all_gather_into_tensor`` collects the
+    slots and ``fs_merge_partials`` merges them.  ``capture`` records the whole step as a
+    CUDA graph (single-rank groups, or any group on the p2p transport).
 
     ``partial_fn(q, cache, (lo, hi)) -> (O, LSE)`` and ``merge_fn(O[N], LSE[N], dtype)``
     replace the CUDA steps (then the generic list all-gather is used); tests run the
     collective logic on CPU ranks (gloo) that way."""
 
     def __init__(self, group: Optional[dist.ProcessGroup] = None,
-                 partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None):
+                 partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
+                 transport: Optional[str] = None, timeout_ms: float = 2000.0):
         self.group = group
         self.partial_fn = partial_fn
         self.merge_fn = merge_fn
+        # multi-rank CUDA steps: "p2p" (peer-memory exchange kernel) or "nccl" (all-gather)
+        self.transport = transport or os.environ.get("FLASHSPEC_EXCHANGE", "p2p")
+        if self.transport not in ("p2p", "nccl"):
+            raise ValueError("transport must be 'p2p' or 'nccl'")
+        self.timeout_ns = int(timeout_ms * 1e6)
         self._bufs = {}
+        self._xch = {}
 
     @property
     def world(self) -> int:
@@ -121,6 +205,12 @@ class SequenceShardedDecoder:
         o = mine[: rows * d].view(b, hq, d)
         lse = mine[rows * d: rows * d + rows].view(b, hq)
         paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages), partial_out=(o, lse))
+        if self.world > 1 and self.transport == "p2p":
+            xkey = (q.device, slot)
+            xch = self._xch.get(xkey)
+            if xch is None:
+                xch = self._xch[xkey] = PeerExchange(self.group, q.device, slot, self.timeout_ns)
+            return xch.merge(o, lse, torch.empty(q.shape, dtype=out_dtype, device=q.device))
         if self.world > 1:  # out of place: the send buffer is not a view of the receive buffer
             dist.all_gather_into_tensor(gather.view(-1), mine, group=self.group)
         else:
@@ -135,10 +225,11 @@ class SequenceShardedDecoder:
     def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16):
         """Record the decode step of a single-rank group (partial kernel + merge) as a CUDA
         graph over the given tensors; returns ``(replay, out)`` where ``replay()`` re-runs
-        the step on the current contents of q / cache and refreshes ``out``.  Steps with a
-        collective are not captured (groups of more than one rank run eagerly)."""
-        if self.world > 1:
-            raise ValueError("capture() is for single-rank groups; multi-rank steps run eagerly")
+        the step on the current contents of q / cache and refreshes ``out``.  Multi-rank
+        steps are captured only with the peer-memory exchange (the NCCL step runs eagerly);
+        every rank must then replay its graph the same number of times."""
+        if self.world > 1 and self.transport != "p2p":
+            raise ValueError("capture() of a multi-rank step needs transport='p2p'; NCCL steps run eagerly")
         side = torch.cuda.Stream(device=q.device)
         side.wait_stream(torch.cuda.current_stream(q.device))
         with torch.cuda.stream(side):

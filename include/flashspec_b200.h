@@ -133,6 +133,48 @@ int fs_paged_decode_noalloc(const FsDecodeArgs* args, void* stream);
 int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_parts, int64_t rows,
                       int32_t head_dim, int64_t part_stride, void* out, int32_t out_dtype, void* stream);
 
+/* Peer-memory exchange for decode steps whose pages are split across the GPUs of one
+ * node (one process per GPU).  It stands where the gather of per-rank partials plus
+ * fs_merge_partials would: the reference has no multi-GPU path, and its combine of
+ * partials (_combine_splits_kernel, src/flashspec/triton_fused.py:446-503) is the
+ * merge applied here to one partial per rank.
+ *
+ * Set-up, once per group: every rank calls fs_exchange_create (a cudaMalloc'd, zeroed
+ * buffer for slots of slot_floats floats -- a multiple of 64, at least
+ * rows*(head_dim+1) -- and its FS_EXCHANGE_HANDLE_BYTES-byte IPC handle), sends the
+ * handle to the other ranks (e.g. through torch.distributed), and maps each peer's
+ * buffer with fs_exchange_open.  Tear-down: fs_exchange_close on the peers' mappings,
+ * then fs_exchange_destroy on its own buffer.
+ *
+ * fs_exchange_merge, per step, on every rank (the same number of calls on each): one
+ * kernel stores this rank's partial rows into every rank's buffer (plain peer stores
+ * over NVLink), raises its flags there, waits for every rank's rows -- up to timeout_ns,
+ * after which it sets FS_DEV_TIMEOUT in device_status and leaves `out` unwritten -- and
+ * writes the merged rows [rows, head_dim] to `out` (FS_F16 or FS_F32).  No host sync and
+ * no collective library call, so a step that uses it can be recorded in a CUDA graph.
+ * After a timeout the buffers' call counters may disagree: recreate them. */
+#define FS_EXCHANGE_MAX_RANKS 8
+#define FS_EXCHANGE_HANDLE_BYTES 64
+typedef struct FsExchangeArgs {
+  int32_t world, rank;
+  void* bufs[FS_EXCHANGE_MAX_RANKS]; /* exchange buffer of every rank, as mapped here */
+  int64_t slot_floats;
+  const float* o_mine;        /* this rank's partial O fp32 [rows, head_dim], 16-byte aligned */
+  const float* lse_mine;      /* this rank's partial LSE fp32 [rows] (natural log)          */
+  int64_t rows;
+  int32_t head_dim;
+  void* out;
+  int32_t out_dtype;
+  int64_t timeout_ns;
+  uint32_t* device_status;    /* optional device word receiving FS_DEV_TIMEOUT           */
+} FsExchangeArgs;
+
+int fs_exchange_create(int64_t slot_floats, void** buf, void* ipc_handle);
+int fs_exchange_open(const void* ipc_handle, void** peer_buf);
+int fs_exchange_close(void* peer_buf);
+int fs_exchange_destroy(void* buf);
+int fs_exchange_merge(const FsExchangeArgs* args, void* stream);
+
 /* Affine INT8 quantization of x [n_lead, seq_len, head_dim] (dtype x_dtype,
  * contiguous) in blocks of block_size tokens, zero-padding the last block:
  * values [n_lead, nblk, block_size, head_dim], scale/zero_point [n_lead, nblk].

@@ -47,7 +47,8 @@ def test_ctypes_layouts_match_c(tmp_path):
     from flashspec_b200 import _lib
 
     structs = {"FsDecodeArgs": _lib.FsDecodeArgs, "FsQuantizeArgs": _lib.FsQuantizeArgs,
-               "FsPageUpdate": _lib.FsPageUpdate, "FsPageUpdateArgs": _lib.FsPageUpdateArgs}
+               "FsPageUpdate": _lib.FsPageUpdate, "FsPageUpdateArgs": _lib.FsPageUpdateArgs,
+               "FsExchangeArgs": _lib.FsExchangeArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')

@@ -1,0 +1,171 @@
+"""The peer-memory exchange of sequence-sharded decode steps (fs_exchange_*).
+
+On one GPU: a one-rank exchange must give exactly fs_merge_partials' result, call
+after call, and a two-rank exchange whose peer never arrives must give up within its
+time limit and say so in the status word (the GPU stays usable).  With two GPUs: two
+ranks (child processes, gloo for the handle exchange) decode their page windows and
+merge through the exchange, eagerly and as CUDA-graph replays, and must match the
+single-GPU decode."""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import socket
+import sys
+import tempfile
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+ATOL, RTOL = 2e-3, 1e-2
+
+pytestmark = pytest.mark.gpu
+
+
+def _need_gpu(n=1):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} CUDA device(s)")
+
+
+def _partial(seed=0):
+    import flashspec_b200 as fs
+    from flashspec_b200 import configs
+
+    wl = configs.paged_workload("xch", 2, 16, 2, [900, 301], seed=seed, device="cuda")
+    o = torch.empty(wl.q.shape, dtype=torch.float32, device="cuda")
+    lse = torch.empty(wl.q.shape[:2], dtype=torch.float32, device="cuda")
+    fs.paged_quant_attention_cuda(wl.q, wl.cache, partial_out=(o, lse))
+    return wl, o, lse
+
+
+def _create(lib, slot):
+    from flashspec_b200 import _lib
+
+    buf, h = C.c_void_p(), (C.c_char * _lib.EXCHANGE_HANDLE_BYTES)()
+    assert lib.fs_exchange_create(slot, C.byref(buf), h) == 0
+    return buf.value
+
+
+def test_one_rank_exchange_equals_merge_partials_on_consecutive_calls():
+    _need_gpu()
+    import flashspec_b200 as fs
+    from flashspec_b200 import _lib
+
+    lib = _lib.load()
+    wl, o, lse = _partial()
+    rows, d = lse.numel(), o.shape[-1]
+    slot = (rows * (d + 1) + 63) // 64 * 64
+    ref = fs.merge_partials(o[None], lse[None], torch.float16)
+    buf = _create(lib, slot)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        a = _lib.FsExchangeArgs()
+        a.world, a.rank = 1, 0
+        a.bufs[0] = buf
+        a.slot_floats, a.rows, a.head_dim = slot, rows, d
+        a.o_mine, a.lse_mine = o.data_ptr(), lse.data_ptr()
+        a.out_dtype, a.timeout_ns, a.device_status = _lib.FS_F16, 10**9, status.data_ptr()
+        stream = torch.cuda.current_stream().cuda_stream
+        for _ in range(3):  # the call counter advances; every call must be complete
+            out = torch.full_like(wl.q, float("nan"))
+            a.out = out.data_ptr()
+            assert lib.fs_exchange_merge(C.byref(a), stream) == 0
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            assert torch.equal(out, ref)
+    finally:
+        torch.cuda.synchronize()
+        lib.fs_exchange_destroy(buf)
+
+
+def test_missing_peer_times_out_and_reports():
+    """Rank 0 of a two-rank exchange whose rank 1 never runs: the kernel waits on a flag
+    nothing sets, gives up after 20 ms, sets FS_DEV_TIMEOUT, and the device stays usable."""
+    _need_gpu()
+    from flashspec_b200 import _lib
+
+    lib = _lib.load()
+    wl, o, lse = _partial()
+    rows, d = lse.numel(), o.shape[-1]
+    slot = (rows * (d + 1) + 63) // 64 * 64
+    mine, silent_peer = _create(lib, slot), _create(lib, slot)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        a = _lib.FsExchangeArgs()
+        a.world, a.rank = 2, 0
+        a.bufs[0], a.bufs[1] = mine, silent_peer
+        a.slot_floats, a.rows, a.head_dim = slot, rows, d
+        a.o_mine, a.lse_mine = o.data_ptr(), lse.data_ptr()
+        out = torch.empty_like(wl.q)
+        a.out, a.out_dtype = out.data_ptr(), _lib.FS_F16
+        a.timeout_ns, a.device_status = 20 * 10**6, status.data_ptr()
+        assert lib.fs_exchange_merge(C.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert int(status.item()) & _lib.FS_DEV_TIMEOUT
+        assert float(torch.ones(4, device="cuda").sum()) == 4.0  # context still usable
+    finally:
+        torch.cuda.synchronize()
+        lib.fs_exchange_destroy(mine)
+        lib.fs_exchange_destroy(silent_peer)
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, out_dir):
+    sys.path.insert(0, str(ROOT))
+    import torch.distributed as dist
+
+    import flashspec_b200 as fs
+    from flashspec_b200 import configs
+    from flashspec_b200.dist import SequenceShardedDecoder
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    wl = configs.paged_workload("xch2", 2, 16, 2, [3000, 1301], seed=5, device=f"cuda:{rank}")
+    n_pages = int(wl.cache.block_table.shape[1])
+    full = fs.paged_quant_attention_cuda(wl.q, wl.cache)
+    dec = SequenceShardedDecoder(transport="p2p")
+    errs = []
+    for _ in range(3):
+        out = dec(wl.q, wl.cache, n_pages)
+        errs.append(float(((out.float() - full.float()).abs() - RTOL * full.float().abs()).max()))
+    replay, gout = dec.capture(wl.q, wl.cache, n_pages)
+    for _ in range(3):
+        replay()
+        torch.cuda.synchronize()
+        errs.append(float(((gout.float() - full.float()).abs() - RTOL * full.float().abs()).max()))
+    torch.cuda.synchronize()
+    status = [int(x.status.item()) for x in dec._xch.values()]
+    (Path(out_dir) / f"rank{rank}.txt").write_text(f"{max(errs)} {max(status)}")
+    dist.barrier()
+    for x in dec._xch.values():
+        x.close()
+    dist.destroy_process_group()
+
+
+def test_two_ranks_match_single_gpu_decode():
+    _need_gpu(2)
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.get_context("spawn")
+        procs = [ctx.Process(target=_rank_main, args=(r, 2, port, d)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+            if p.is_alive():
+                p.kill()
+        assert [p.exitcode for p in procs] == [0, 0]
+        for r in range(2):
+            err, status = (Path(d) / f"rank{r}.txt").read_text().split()
+            assert float(err) <= ATOL and int(status) == 0, (r, err, status)
