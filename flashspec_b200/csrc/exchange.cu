@@ -7,16 +7,17 @@
 // rank owns one exchange buffer (cudaMalloc'd here and shared by CUDA IPC handle); every
 // rank maps every peer's buffer.  One kernel per step: CTA c takes a slice of rows,
 // stores them (plain peer stores over NVLink, no multicast) into every rank's buffer,
-// raises its flag there, waits with a time limit for the same slice's flags from all
-// ranks, and merges the slice locally.
+// and merges the slice locally as every rank's words for it arrive, waiting at most
+// timeout_ns.
 //
-// Buffer layout (bytes): [0, 256) control words (epoch = calls completed, done = CTAs
-// finished in the current call); [256, 256 + 4 * kXMaxRanks * kXMaxCtas) flags
-// [sender][cta] = epoch the sender's slice belongs to; then the data, two epoch
-// parities x kXMaxRanks slots of slot_floats floats (O [rows][D], then LSE [rows]).
-// Parity: a peer may begin its next call as soon as it has this rank's flags, so its next
-// rows land in the other parity while this rank still reads the current one; it cannot
-// get two calls ahead, as that needs this rank's flags of the next call.
+// Protocol: every value travels as one naturally aligned 8-byte word, (value bits,
+// call epoch) -- single-copy atomic -- so a receiver knows a word has arrived when its
+// tag equals the current epoch, without fences or separate flags.  Buffer layout
+// (bytes): [0, 256) per-CTA call counters (epoch of CTA c's last completed call); then
+// two epoch parities x kXMaxRanks slots of slot_floats words (O [rows][D], then LSE
+// [rows]).  Parity: a peer may begin its next call as soon as it has this rank's words,
+// so its next words land in the other parity while this rank still reads the current
+// one; it cannot get two calls ahead, as that needs this rank's words of the next call.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -31,101 +32,94 @@ namespace fsb {
 constexpr int kXMaxRanks = FS_EXCHANGE_MAX_RANKS;
 constexpr int kXMaxCtas = 64;
 constexpr int kXThreads = 256;
-constexpr size_t kXCtrlBytes = 256;
-constexpr size_t kXFlagBytes = 4ull * kXMaxRanks * kXMaxCtas;
-constexpr size_t kXDataOffset = kXCtrlBytes + kXFlagBytes;
+constexpr size_t kXCtrlBytes = 256;  // kXMaxCtas 32-bit call counters
+constexpr size_t kXDataOffset = kXCtrlBytes;
+static_assert(kXMaxCtas * 4 <= kXCtrlBytes, "call counters");
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t tag) {
+  const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+
+// Value of the word at p once it carries tag e; false when the deadline passes first.
+__device__ __forceinline__ bool wait_word(const uint64_t* p, uint32_t e, uint64_t deadline, float& v) {
+  for (unsigned n = 0;; ++n) {
+    const uint64_t w = ld_word(p);
+    if ((uint32_t)(w >> 32) == e) {
+      v = __uint_as_float((uint32_t)w);
+      return true;
+    }
+    if ((n & 255u) == 255u && globaltimer_ns() > deadline) return false;
+  }
 }
 
 __global__ void __launch_bounds__(kXThreads) exchange_merge_kernel(const FsExchangeArgs a, int rows_per_cta) {
-  __shared__ int s_ok;
-  __shared__ uint32_t s_epoch;
   const int tid = threadIdx.x, c = blockIdx.x;
   const int D = a.head_dim;
   const int64_t r0 = (int64_t)c * rows_per_cta;
   const int64_t r1 = r0 + rows_per_cta < a.rows ? r0 + rows_per_cta : a.rows;
   uint8_t* own = static_cast<uint8_t*>(a.bufs[a.rank]);
-  uint32_t* ctrl = reinterpret_cast<uint32_t*>(own);
-  if (tid == 0) s_epoch = ld_acquire_sys(ctrl) + 1u;  // the call this launch is
-  __syncthreads();
-  const uint32_t e = s_epoch;
-  const size_t parity_off = kXDataOffset + (size_t)(e & 1u) * kXMaxRanks * a.slot_floats * 4;
+  uint32_t* calls = reinterpret_cast<uint32_t*>(own);
+  const uint32_t e = calls[c] + 1u;  // written by this CTA's previous call on this GPU
+  const size_t parity_off = kXDataOffset + (size_t)(e & 1u) * kXMaxRanks * a.slot_floats * 8;
+  const int64_t lse_at = a.rows * D;
+  const uint64_t deadline = globaltimer_ns() + (uint64_t)a.timeout_ns;
 
-  // 1. this rank's rows of the slice into slot [rank] of every rank's buffer
-  const int64_t nO = (r1 - r0) * D;
+  // 1. this rank's rows of the slice, tagged, into slot [rank] of every rank's buffer
   for (int p = 0; p < a.world; ++p) {
-    float* dst = reinterpret_cast<float*>(static_cast<uint8_t*>(a.bufs[p]) + parity_off) + (size_t)a.rank * a.slot_floats;
-    for (int64_t i = tid; i < nO / 4; i += kXThreads)
-      reinterpret_cast<float4*>(dst + r0 * D)[i] = reinterpret_cast<const float4*>(a.o_mine + r0 * D)[i];
-    for (int64_t r = r0 + tid; r < r1; r += kXThreads) dst[a.rows * D + r] = a.lse_mine[r];
+    uint64_t* dst = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(a.bufs[p]) + parity_off) +
+                    (size_t)a.rank * a.slot_floats;
+    for (int64_t i = r0 * D + tid; i < r1 * D; i += kXThreads) st_word(dst + i, a.o_mine[i], e);
+    for (int64_t r = r0 + tid; r < r1; r += kXThreads) st_word(dst + lse_at + r, a.lse_mine[r], e);
   }
-  __threadfence_system();  // this thread's stores are visible system-wide before the flags
   __syncthreads();
-  // 2. raise this slice's flag in every rank's buffer
-  if (tid < a.world) {
-    uint32_t* fl = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a.bufs[tid]) + kXCtrlBytes);
-    st_release_sys(fl + a.rank * kXMaxCtas + c, e);
-  }
-  // 3. wait (bounded) for the slice's flags of every rank
-  if (tid == 0) s_ok = 1;
-  __syncthreads();
-  if (tid < a.world) {
-    const uint32_t* fl = reinterpret_cast<const uint32_t*>(own + kXCtrlBytes) + tid * kXMaxCtas + c;
-    const uint64_t t0 = globaltimer_ns();
-    while ((int32_t)(ld_acquire_sys(fl) - e) < 0) {  // a peer may already be one call ahead
-      if (globaltimer_ns() - t0 > (uint64_t)a.timeout_ns) {
-        s_ok = 0;
-        if (a.device_status != nullptr) atomicOr(a.device_status, FS_DEV_TIMEOUT);
-        break;
+  // 2. merge the slice as the words arrive: out = sum_p w_p O_p / sum_p w_p,
+  //    w_p = exp(lse_p - max lse) (triton_fused.py:446-503 on one partial per rank)
+  const uint64_t* data = reinterpret_cast<const uint64_t*>(own + parity_off);
+  bool ok = true;
+  for (int64_t i = r0 * D + tid; i < r1 * D && ok; i += kXThreads) {
+    const int64_t row = i / D;
+    float lse[kXMaxRanks], o[kXMaxRanks];
+    float M = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < kXMaxRanks; ++p) {
+      lse[p] = -INFINITY;
+      o[p] = 0.f;
+      if (p < a.world && ok) {
+        ok = wait_word(data + (size_t)p * a.slot_floats + lse_at + row, e, deadline, lse[p]) &&
+             wait_word(data + (size_t)p * a.slot_floats + i, e, deadline, o[p]);
+        M = fmaxf(M, lse[p]);
       }
-      __nanosleep(64);
     }
-  }
-  __syncthreads();
-  // 4. merge the slice from the local buffer: out = sum_r w_r O_r / sum_r w_r,
-  //    w_r = exp(lse_r - max lse) (triton_fused.py:446-503 on one partial per rank)
-  if (s_ok) {
-    const float* data = reinterpret_cast<const float*>(own + parity_off);
-    for (int64_t i = r0 * D + tid; i < r1 * D; i += kXThreads) {
-      const int64_t row = i / D;
-      float M = -INFINITY;
-      for (int p = 0; p < a.world; ++p) M = fmaxf(M, data[(size_t)p * a.slot_floats + a.rows * D + row]);
-      float W = 0.f, O = 0.f;
-      if (M != -INFINITY)
-        for (int p = 0; p < a.world; ++p) {
-          const float l = data[(size_t)p * a.slot_floats + a.rows * D + row];
-          const float w = l == -INFINITY ? 0.f : expf(l - M);
+    if (!ok) break;
+    float W = 0.f, O = 0.f;
+    if (M != -INFINITY)
+#pragma unroll
+      for (int p = 0; p < kXMaxRanks; ++p)
+        if (p < a.world) {
+          const float w = lse[p] == -INFINITY ? 0.f : expf(lse[p] - M);
           W += w;
-          O += w * data[(size_t)p * a.slot_floats + i];
+          O += w * o[p];
         }
-      const float o = W > 0.f ? O / W : 0.f;
-      if (a.out_dtype == FS_F16)
-        static_cast<__half*>(a.out)[i] = __float2half_rn(o);
-      else
-        static_cast<float*>(a.out)[i] = o;
-    }
+    const float v = W > 0.f ? O / W : 0.f;
+    if (a.out_dtype == FS_F16)
+      static_cast<__half*>(a.out)[i] = __float2half_rn(v);
+    else
+      static_cast<float*>(a.out)[i] = v;
   }
-  // 5. the last CTA out records the completed call
+  if (!ok && a.device_status != nullptr) atomicOr(a.device_status, FS_DEV_TIMEOUT);
+  // 3. record the completed call (read by this CTA's next call on this GPU)
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(ctrl + 1, 1u) == gridDim.x - 1) {
-      ctrl[1] = 0u;
-      __threadfence();
-      st_release_sys(ctrl, e);
-    }
-  }
+  if (tid == 0) calls[c] = e;
 }
 
-size_t exchange_bytes(int64_t slot_floats) { return kXDataOffset + 2ull * kXMaxRanks * (size_t)slot_floats * 4; }
+size_t exchange_bytes(int64_t slot_floats) { return kXDataOffset + 2ull * kXMaxRanks * (size_t)slot_floats * 8; }
 
 }  // namespace fsb
 

@@ -140,17 +140,17 @@ int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_pa
  * merge applied here to one partial per rank.
  *
  * Set-up, once per group: every rank calls fs_exchange_create (a cudaMalloc'd, zeroed
- * buffer for slots of slot_floats floats -- a multiple of 64, at least
- * rows*(head_dim+1) -- and its FS_EXCHANGE_HANDLE_BYTES-byte IPC handle), sends the
+ * buffer for slots of slot_floats elements -- a multiple of 64, at least
+ * rows*(head_dim+1); each element travels as an 8-byte (value, call tag) word -- and its FS_EXCHANGE_HANDLE_BYTES-byte IPC handle), sends the
  * handle to the other ranks (e.g. through torch.distributed), and maps each peer's
  * buffer with fs_exchange_open.  Tear-down: fs_exchange_close on the peers' mappings,
  * then fs_exchange_destroy on its own buffer.
  *
  * fs_exchange_merge, per step, on every rank (the same number of calls on each): one
  * kernel stores this rank's partial rows into every rank's buffer (plain peer stores
- * over NVLink), raises its flags there, waits for every rank's rows -- up to timeout_ns,
- * after which it sets FS_DEV_TIMEOUT in device_status and leaves `out` unwritten -- and
- * writes the merged rows [rows, head_dim] to `out` (FS_F16 or FS_F32).  No host sync and
+ * over NVLink) and waits for every rank's rows -- up to timeout_ns, after which it sets
+ * FS_DEV_TIMEOUT in device_status and leaves the rest of `out` unwritten -- and writes
+ * the merged rows [rows, head_dim] to `out` (FS_F16 or FS_F32).  No host sync and
  * no collective library call, so a step that uses it can be recorded in a CUDA graph.
  * After a timeout the buffers' call counters may disagree: recreate them. */
 #define FS_EXCHANGE_MAX_RANKS 8
