@@ -340,7 +340,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     tb = cache.block_table.numel() * 8
     lb = cache.lengths.numel() * 8
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if seqshard:
+    if seqshard and not graphable:
         q_host = q.cpu().pin_memory()
         table_host = cache.block_table.cpu().pin_memory()
         lengths_host = cache.lengths.cpu().pin_memory()
@@ -348,21 +348,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         q_dev, table_dev, lengths_dev = torch.empty_like(q), torch.empty_like(cache.block_table), torch.empty_like(cache.lengths)
         cache_e2e = fs.PagedKVCache(cache.k_quant, cache.v_quant, table_dev, lengths_dev, cache.block_size,
                                     cache.max_seq_len)
-        if graphable:
-            q_dev.copy_(q)
-            table_dev.copy_(cache.block_table)
-            lengths_dev.copy_(cache.lengths)
-            replay_e2e, out_e2e = decoder.capture(q_dev, cache_e2e, n_pages)
 
         def e2e_step(i):
             q_dev.copy_(q_host, non_blocking=True)
             table_dev.copy_(table_host, non_blocking=True)
             lengths_dev.copy_(lengths_host, non_blocking=True)
-            if graphable:
-                replay_e2e()
-                out = out_e2e
-            else:
-                out = decoder(q_dev, cache_e2e, n_pages)
+            out = decoder(q_dev, cache_e2e, n_pages)
             out_host.copy_(out, non_blocking=True)
     else:
         n_in = qb + tb + lb
@@ -384,6 +375,17 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         h2d_done = [torch.cuda.Event() for _ in range(2)]
         kern_done = [torch.cuda.Event() for _ in range(2)]
+        if seqshard:  # one captured decoder step (decode + exchange) per input buffer
+            graphs = []
+            for b in range(2):
+                dev_in[b].copy_(host_in[b])
+                graphs.append(decoder.capture(q_in[b], caches[b], n_pages))
+
+        def run(b):
+            if seqshard:
+                graphs[b][0]()
+                return graphs[b][1]
+            return fs.paged_quant_attention_cuda(q_in[b], caches[b], num_splits=splits)
 
         def pipelined_step(i, cur):
             b = i % 2
@@ -395,7 +397,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 dev_in[b].copy_(host_in[b], non_blocking=True)
                 h2d_done[b].record(h2d_stream)
             cur.wait_event(h2d_done[b])
-            out = fs.paged_quant_attention_cuda(q_in[b], caches[b], num_splits=splits)
+            out = run(b)
             kern_done[b].record(cur)
             d2h_stream.wait_event(kern_done[b])
             with torch.cuda.stream(d2h_stream):
@@ -406,21 +408,27 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             pipelined_step(i, stream)
         stream.wait_stream(d2h_stream)
         torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            cap = torch.cuda.current_stream()
-            for i in range(kGraphSteps):
-                pipelined_step(i, cap)
-            cap.wait_stream(h2d_stream)
-            cap.wait_stream(d2h_stream)
-        e2e_steps = max(kGraphSteps, e2e_steps // kGraphSteps * kGraphSteps)
+        if seqshard:  # steps are already graph replays: issued eagerly, in pipeline
+            def e2e_step(i):
+                pipelined_step(i + 4, stream)
+                if i == e2e_steps - 1:
+                    stream.wait_stream(d2h_stream)
+        else:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                cap = torch.cuda.current_stream()
+                for i in range(kGraphSteps):
+                    pipelined_step(i, cap)
+                cap.wait_stream(h2d_stream)
+                cap.wait_stream(d2h_stream)
+            e2e_steps = max(kGraphSteps, e2e_steps // kGraphSteps * kGraphSteps)
 
-        def e2e_step(i):
-            if i % kGraphSteps == 0:
-                graph.replay()
+            def e2e_step(i):
+                if i % kGraphSteps == 0:
+                    graph.replay()
 
     for i in range(3):
-        e2e_step(i if seqshard else 0)
+        e2e_step(i if (seqshard and not graphable) else 0)
     barrier()
     e0.record(stream)
     for i in range(e2e_steps):
@@ -466,7 +474,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "us_per_call": e2e_ms / e2e_steps * 1e3,
                 "api": ("flashspec_b200 sequence-sharded decoder, q/table/lengths copied from pinned host and "
-                        "the output read back serially every step" if seqshard else
+                        "the output read back serially every step" if (seqshard and not graphable) else
+                        "flashspec_b200 sequence-sharded decoder, each step a CUDA-graph replay of decode + exchange; "
+                        "every step one packed H2D of q/table/lengths from pinned host (side stream, double-buffered) "
+                        "and its output read back (second side stream), overlapping the neighbouring steps" if seqshard else
                         "flashspec_b200.paged_quant_attention_cuda replayed from a CUDA graph of 10 steps; every "
                         "step one packed H2D of q/table/lengths from pinned host (side stream, double-buffered) "
                         "and its output read back (second side stream), overlapping the neighbouring steps' decode")},
