@@ -222,6 +222,17 @@ class SequenceShardedDecoder:
                                                  code, stream_of(q.device)), "fs_merge_partials")
         return out
 
+    def close(self) -> None:
+        """Release the peer-exchange buffers (collectively: every rank calls it, after its
+        last step has finished on the GPU; further calls set them up again)."""
+        if self._xch:
+            torch.cuda.synchronize()
+            if dist.is_initialized() and self.world > 1:
+                dist.barrier(group=self.group)  # no peer still writes into a buffer we free
+            for x in self._xch.values():
+                x.close()
+            self._xch.clear()
+
     def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16):
         """Record the decode step of a single-rank group (partial kernel + merge) as a CUDA
         graph over the given tensors; returns ``(replay, out)`` where ``replay()`` re-runs

@@ -145,9 +145,7 @@ def _rank_main(rank, world, port, out_dir):
     torch.cuda.synchronize()
     status = [int(x.status.item()) for x in dec._xch.values()]
     (Path(out_dir) / f"rank{rank}.txt").write_text(f"{max(errs)} {max(status)}")
-    dist.barrier()
-    for x in dec._xch.values():
-        x.close()
+    dec.close()
     dist.destroy_process_group()
 
 
