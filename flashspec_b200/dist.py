@@ -121,14 +121,24 @@ class PeerExchange:
         _lib.check(self._lib.fs_exchange_merge(C.byref(a), stream_of(self.device)), "fs_exchange_merge")
         return out
 
-    def close(self) -> None:
+    def close_peers(self) -> None:
+        """Unmap the peers' buffers (this rank stops addressing them)."""
         with torch.cuda.device(self.device):
             for p in self._peers:
                 self._lib.fs_exchange_close(p)
-            self._peers = []
+        self._peers = []
+
+    def destroy(self) -> None:
+        """Free this rank's own buffer: only after every peer has unmapped it."""
+        with torch.cuda.device(self.device):
             if self._own:
                 self._lib.fs_exchange_destroy(self._own)
                 self._own = None
+
+    def close(self) -> None:
+        """Single-process teardown (no peer holds this rank's buffer)."""
+        self.close_peers()
+        self.destroy()
 
 
 class SequenceShardedDecoder:
@@ -227,10 +237,15 @@ class SequenceShardedDecoder:
         last step has finished on the GPU; further calls set them up again)."""
         if self._xch:
             torch.cuda.synchronize()
-            if dist.is_initialized() and self.world > 1:
-                dist.barrier(group=self.group)  # no peer still writes into a buffer we free
+            multi = dist.is_initialized() and self.world > 1
+            if multi:
+                dist.barrier(group=self.group)  # every rank's last exchange has finished
             for x in self._xch.values():
-                x.close()
+                x.close_peers()
+            if multi:
+                dist.barrier(group=self.group)  # every rank has unmapped its peers' buffers
+            for x in self._xch.values():
+                x.destroy()
             self._xch.clear()
 
     def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16):
