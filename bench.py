@@ -1,33 +1,38 @@
-"""Benchmark of the paged INT8 decode-attention hot path (driver contract).
+"""Benchmark of the INT8 decode-attention hot path (driver contract).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg1]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config cfg0|cfg1|cfg2|cfg3|cfg4]
 
 A step is one decode-attention call over the configuration's whole batch.  The
 default workload is BASELINE configs[1] (cfg1): paged INT8 KV, B16, 32 Q/KV heads,
-D128, seq 4096, page 16, pool = 4096 pages + 10% slack, shuffled block_table.
-Inputs are larger than L2 (539 MB of KV), so no flush is needed between steps.
+D128, seq 4096, page 16, pool = 4096 pages + 10% slack, shuffled block_table.  Its
+539 MB of KV is larger than L2 (126 MB), so no flush is needed between steps; cfg0
+(135 MB) rotates over four copies of its inputs instead.
 
-ours (default): KV pool, q and the table are resident in HBM; K timed steps of
-``paged_quant_attention_cuda`` between CUDA events (barrier + synchronize on both
-sides; N>1 = independent per-rank shards, max time over ranks).  ``value`` is the
+ours (default): inputs resident in HBM; K timed steps between CUDA events on the
+launching stream (barrier + synchronize on both sides; N>1 = independent per-rank
+request shards of the same configuration, max time over ranks).  ``value`` is the
 aggregate algorithmic bandwidth (bytes every rank's calls must move / time).
-``e2e`` times the same public call with the per-step inputs (q, block_table,
-lengths) copied from pinned host memory and the output copied back, every step
-(copies double-buffered on side streams and steps replayed from a CUDA graph, so
-the copies overlap neighbouring steps' decode).  ``roofline`` divides the kernel's
-achieved bytes/s (per-launch CUDA events, in a second pass outside the timed loop)
-by the measured HBM copy peak.  ``cpu_baseline`` times the CPU oracle (a numpy port of
-the reference's ``paged_quant_attention``) on a bounded sample of the same data.
+``roofline`` divides the decode kernel's algorithmic bytes per launch by its mean
+launch time over that timed region and compares with the measured copy peak, the
+read-only stream peak measured in the same run, and 8 TB/s nominal.  ``e2e`` times the
+public call with the per-step inputs (q, block_table, lengths) copied from pinned host
+memory and the output copied back every step.  Two sub-objects accompany cfg1:
+``paged_vs_contiguous`` (the same KV laid out contiguously, through the fused entry
+point, timed in the same run) and ``seqshard`` (cfg3, the 131072-token requests split
+by page windows across the N ranks with the peer-memory exchange, plus an in-run check
+of rank 0's merged output against a single-GPU decode of the whole sequence).
+``cpu_baseline`` times the CPU reference arm on the box's host cores.
 
-reference: times that CPU port on the box's host cores over a bounded sample per
-step (rank 0 only under torchrun) and reports the same metric.
+reference: ``oracle/torch_reference.py`` -- the reference's CPU ``fused``/``paged``
+backends restated op for op in torch -- on host-built inputs of the same configuration
+(never the CUDA library), whole calls, all host cores, rank 0 only under torchrun.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -41,6 +46,8 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "decode-attn µs/call & achieved HBM TB/s (frac of B200 peak), paged INT8 KV"
 FALLBACK_HBM_GBS = 6650.0
+NOMINAL_HBM_GBS = 8000.0
+REFERENCE_BUDGET_S = 60.0  # timed CPU work of the reference arm, at most (3 calls minimum)
 
 
 def parse_args():
@@ -49,9 +56,11 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
+    ap.add_argument("--config", choices=["cfg0", "cfg1", "cfg2", "cfg3", "cfg4"], default="cfg1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-soak", action="store_true", help="skip the 1.5 s clock soak (for profiler launch lists)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the paged_vs_contiguous / seqshard sub-objects and the read probe")
     return ap.parse_args()
 
 
@@ -69,16 +78,19 @@ def measured_peaks():
 
 
 def traffic_per_launch(config: str):
-    """Per-launch DRAM bytes (read + write) of the decode kernel from the committed ncu
-    summary, or None."""
+    """(DRAM bytes read + written per launch, source) of the decode kernel for this
+    configuration from the committed ncu summary, or (None, None)."""
     p = ROOT / "profiles" / "traffic_per_launch.txt"
     if not p.exists():
-        return None
+        return None, None
+    source = None
     for line in p.read_text().splitlines():
+        if line.startswith("# source:"):
+            source = line[len("# source:"):].strip()
         parts = line.split()
         if len(parts) >= 2 and parts[0] == config:
-            return int(float(parts[1]))
-    return None
+            return int(float(parts[1])), source or "profiles/traffic_per_launch.txt"
+    return None, None
 
 
 class ClockSampler:
@@ -141,10 +153,279 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def build_workload(config: str, rank: int, world: int = 1):
+def torch_reference():
+    """The CPU reference arm module (measurement infrastructure under oracle/)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import torch_reference as T
+
+    return T
+
+
+def use_all_host_cores() -> int:
+    """torchrun sets OMP_NUM_THREADS=1; the CPU arms use every host core explicitly."""
+    import torch
+
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def time_cpu_calls(call, warmup: int, steps_requested: int, budget_s: float = REFERENCE_BUDGET_S):
+    """Untimed warm-up calls, then whole timed calls until ``steps_requested`` are done or
+    the budget is spent (at least 3).  Returns (seconds per call list)."""
+    for _ in range(warmup):
+        call()
+    ts, spent = [], 0.0
+    while len(ts) < max(1, steps_requested) and (len(ts) < 3 or spent < budget_s):
+        t0 = time.perf_counter()
+        call()
+        ts.append(time.perf_counter() - t0)
+        spent += ts[-1]
+    return ts
+
+
+def cpu_reference_line(config: str, warmup: int, steps: int, budget_s: float = REFERENCE_BUDGET_S):
+    """Time the torch-CPU reference path on host-built inputs of ``config``."""
+    T = torch_reference()
+    cores = use_all_host_cores()
+    t_build = time.perf_counter()
+    wl = T.host_workload(config)
+    t_build = time.perf_counter() - t_build
+    ts = time_cpu_calls(wl.call, warmup, steps, budget_s)
+    per_call = sum(ts) / len(ts)
+    return wl, ts, per_call, cores, t_build
+
+
+# ------------------------------------------------------------------------------------
+# reference arm
+# ------------------------------------------------------------------------------------
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    if args.config == "cfg4":
+        run_serving_reference(args)
+        return
+    warm = min(args.warmup, 1)
+    wl, ts, per_call, cores, t_build = cpu_reference_line(args.config, warm, args.steps)
+    value = wl.bytes_per_call / per_call / 1e12
+    sample = (f"whole calls of {wl.name} (all {len(wl.lengths)} requests, inputs built on the host in "
+              f"{t_build:.1f} s, not timed): {len(ts)} timed calls after {warm} warm-up; at most "
+              f"{REFERENCE_BUDGET_S:.0f} s of timed calls (minimum 3), so steps may be fewer than requested")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": len(ts), "steps_requested": args.steps, "warmup": warm, "warmup_requested": args.warmup,
+        "ms_per_step": per_call * 1e3, "us_per_call": per_call * 1e6,
+        "tokens_per_s": len(wl.lengths) / per_call, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 KV, fp16 q/out, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": wl.name, "global_batch": len(wl.lengths), "seq_len": max(wl.lengths),
+                   "parallelism": "cpu (rank 0 only)", "bytes_per_call": wl.bytes_per_call},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample,
+                         "os_cpu_count": os.cpu_count(), "torch_threads": cores,
+                         "impl": "oracle/torch_reference.py: reference fused/paged CPU backends restated in torch"},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "call_s": ts,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_serving_reference(args):
+    """cfg4 at reduced scale on the CPU reference allocator (oracle/torch_reference.py)."""
+    T = torch_reference()
+    cores = use_all_host_cores()
+    res = T.serving_loop(T.ServingParams())
+    value = res["bytes_moved"] / res["loop_s"] / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus,
+        "steps": res["steps"], "steps_requested": args.steps, "warmup": 0, "ms_per_step": res["loop_s"] / res["steps"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 KV, fp16 q/out/tokens, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "cfg4_serving_loop (reduced scale)", "parallelism": "cpu (rank 0 only)",
+                   **res["params"]},
+        "serving": res,
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port",
+                         "sample": "reduced-scale serving loop (see config): the full-scale allocator needs more "
+                                   "than 60 GB of host memory and hours of CPU time",
+                         "os_cpu_count": os.cpu_count(), "torch_threads": cores},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------
+
+
+class Timer:
+    """Device time of ``steps`` calls on one stream (barrier + synchronize on both
+    sides, max over ranks)."""
+
+    def __init__(self, dev, world):
+        import torch
+
+        self.dev, self.world = dev, world
+        self.stream = torch.cuda.current_stream(dev)
+
+    def barrier(self):
+        import torch
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, ms: float) -> float:
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([ms], dtype=torch.float64, device=self.dev)
+        if self.world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def run(self, step, steps: int) -> float:
+        import torch
+
+        self.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(self.stream)
+        for i in range(steps):
+            step(i)
+        b.record(self.stream)
+        self.barrier()
+        return self.max_over_ranks(a.elapsed_time(b))
+
+
+def host_us_per_call(call, n: int = 50) -> float:
+    """Host-side cost of issuing one call (validation, plan, tensor maps, launch): the
+    wall time of issuing n calls right after a synchronize, before the queue fills."""
+    import torch
+
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(n):
+        call()
+    t1 = time.perf_counter()
+    torch.cuda.synchronize()
+    return (t1 - t0) / n * 1e6
+
+
+class E2EPipeline:
+    """Per-step host<->device traffic through the public API: every step copies its
+    inputs (packed into one pinned host buffer) to one of two device buffers on a side
+    stream and reads its output back on a second side stream, so neighbouring steps'
+    copies overlap this step's decode, as a serving loop arranges it.  ``make_run(b,
+    views)`` returns the call that consumes device buffer b's views and returns its
+    output tensor."""
+
+    def __init__(self, dev, host_tensors, make_run, out_like):
+        import torch
+
+        self.dev = dev
+        sizes = [t.numel() * t.element_size() for t in host_tensors]
+        self.h2d_bytes = sum(sizes)
+        self.d2h_bytes = out_like.numel() * out_like.element_size()
+        self.host_in, self.dev_in, self.runs, self.outs_host = [], [], [], []
+        for b in range(2):
+            h = torch.empty(self.h2d_bytes, dtype=torch.uint8).pin_memory()
+            views, off = [], 0
+            d = torch.empty(self.h2d_bytes, dtype=torch.uint8, device=dev)
+            for t, n in zip(host_tensors, sizes):
+                h[off:off + n].copy_(t.cpu().contiguous().view(-1).view(torch.uint8))
+                views.append(d[off:off + n].view(t.dtype).view(t.shape))
+                off += n
+            self.host_in.append(h)
+            self.dev_in.append(d)
+            d.copy_(h)
+            self.runs.append(make_run(b, views))
+            self.outs_host.append(torch.empty(out_like.shape, dtype=out_like.dtype).pin_memory())
+        self.h2d = torch.cuda.Stream(dev)
+        self.d2h = torch.cuda.Stream(dev)
+        self.h2d_done = [torch.cuda.Event() for _ in range(2)]
+        self.kern_done = [torch.cuda.Event() for _ in range(2)]
+
+    def step(self, i, cur):
+        import torch
+
+        b = i % 2
+        if i < 2:  # the first step of each buffer forks from the compute stream
+            self.h2d.wait_stream(cur)
+        else:
+            self.h2d.wait_event(self.kern_done[b])
+        with torch.cuda.stream(self.h2d):
+            self.dev_in[b].copy_(self.host_in[b], non_blocking=True)
+            self.h2d_done[b].record(self.h2d)
+        cur.wait_event(self.h2d_done[b])
+        out = self.runs[b]()
+        self.kern_done[b].record(cur)
+        self.d2h.wait_event(self.kern_done[b])
+        with torch.cuda.stream(self.d2h):
+            self.outs_host[b].copy_(out, non_blocking=True)
+
+    def graph(self, steps: int):
+        """Capture ``steps`` pipelined steps as one CUDA graph (so the host's per-step
+        stream/event/copy calls do not pace the GPU); returns its replay."""
+        import torch
+
+        stream = torch.cuda.current_stream(self.dev)
+        for i in range(4):  # eager warm-up: workspaces, tickets, kernel configuration
+            self.step(i, stream)
+        stream.wait_stream(self.d2h)
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            cap = torch.cuda.current_stream()
+            for i in range(steps):
+                self.step(i, cap)
+            cap.wait_stream(self.h2d)
+            cap.wait_stream(self.d2h)
+        return g.replay
+
+
+def read_probe_gbs(dev, gib: float = 4.0, reps: int = 5) -> float:
+    """Best-of-reps read-only HBM bandwidth (fs_read_bandwidth_probe over a buffer far
+    larger than L2)."""
+    import ctypes as C
+
+    import torch
+
+    from flashspec_b200 import _lib
+    from flashspec_b200.quant import stream_of
+
+    lib = _lib.load()
+    nbytes = int(gib * (1 << 30))
+    buf = torch.ones(nbytes // 4, dtype=torch.int32, device=dev)
+    sink = torch.zeros(1 << 16, dtype=torch.int32, device=dev)
+    used = C.c_int32(0)
+    stream = stream_of(dev)
+
+    def call():
+        _lib.check(lib.fs_read_bandwidth_probe(buf.data_ptr(), nbytes, sink.data_ptr(), sink.numel(), C.byref(used),
+                                               stream), "fs_read_bandwidth_probe")
+
+    call()
+    best = 0.0
+    s = torch.cuda.current_stream(dev)
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        call()
+        b.record(s)
+        b.synchronize()
+        best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+    del buf
+    torch.cuda.empty_cache()
+    return best
+
+
+def build_workload(config: str, rank: int, world: int):
     from flashspec_b200 import configs
 
     seed = 1000 * rank
+    if config == "cfg0":
+        return configs.cfg0(seed=seed)
     if config == "cfg1":
         return configs.cfg1(seed=seed)
     if config == "cfg2":
@@ -152,347 +433,291 @@ def build_workload(config: str, rank: int, world: int = 1):
     return configs.cfg3_shard(rank, world)
 
 
-# ------------------------------------------------------------------------------------
-# CPU baseline: numpy port of the reference paged path on a bounded sample
-# ------------------------------------------------------------------------------------
+def contiguous_copy(wl):
+    """The paged workload's KV gathered into the contiguous (fused) layout: values
+    [B, H, nblk, 16, D] in logical page order, qparams [B, H, nblk] (all requests full)."""
+    import flashspec_b200 as fs
 
+    t = wl.cache.block_table
 
-def cpu_sample(wl, n_req: int):
-    """Host copy of the first n_req requests of the workload: their pages only, as an
-    oracle cache (the reference dequantizes the whole pool it is given)."""
-    import numpy as np
+    def gather(qt):
+        v = qt.values[t].squeeze(3).permute(0, 2, 1, 3, 4).contiguous()  # [B, H, nblk, 16, D]
+        s = qt.scale[t].squeeze(-1).squeeze(-1).squeeze(-1).permute(0, 2, 1).contiguous()
+        z = qt.zero_point[t].squeeze(-1).squeeze(-1).squeeze(-1).permute(0, 2, 1).contiguous()
+        b, h, n = s.shape
+        return fs.QuantizedTensor(v, s.view(b, h, n, 1, 1), z.view(b, h, n, 1, 1), 16, (b, h, n * 16, 128))
 
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import flashspec_oracle as O
-
-    table = wl.cache.block_table[:n_req].cpu().numpy()
-    used = np.unique(table[table >= 0])
-    remap = np.full(int(used.max()) + 1, -1, np.int64)
-    remap[used] = np.arange(used.size)
-    import torch
-
-    idx = torch.from_numpy(used).to(wl.cache.k_quant.values.device)
-
-    def sub(qt):
-        return O.OQuant(qt.values[idx].cpu().numpy(), qt.scale[idx].cpu().numpy(), qt.zero_point[idx].cpu().numpy(),
-                        16, (used.size,) + tuple(qt.original_shape[1:]))
-
-    t = np.where(table >= 0, remap[np.maximum(table, 0)], -1)
-    lengths = np.array(wl.lengths[:n_req], np.int64)
-    cache = O.OPagedCache(sub(wl.cache.k_quant), sub(wl.cache.v_quant), t, lengths, 16, int(lengths.max()))
-    q = wl.q[:n_req].cpu().numpy()
-    return O, q, cache
-
-
-def cpu_threads() -> int:
-    try:
-        from threadpoolctl import threadpool_info
-
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return 1
-
-
-def time_cpu_baseline(wl, n_req: int, reps: int):
-    O, q, cache = cpu_sample(wl, n_req)
-    O.paged_quant_attention(q, cache)  # warm-up
-    ts = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        O.paged_quant_attention(q, cache)
-        ts.append(time.perf_counter() - t0)
-    t = statistics.median(ts)
-    frac = sum((n + 15) // 16 for n in wl.lengths[:n_req]) / sum((n + 15) // 16 for n in wl.lengths)
-    full_s = t / frac  # the sample's share of the call's pages
-    return full_s, ts
-
-
-# ------------------------------------------------------------------------------------
-# arms
-# ------------------------------------------------------------------------------------
-
-
-def run_reference(args, rank: int, world: int):
-    if rank != 0:
-        return
-    import torch  # noqa: F401  (device-free)
-
-    os.environ.setdefault("CUDA_VISIBLE_DEVICES", os.environ.get("CUDA_VISIBLE_DEVICES", ""))
-    wl = build_workload(args.config, 0)
-    n_req = 2 if args.config != "cfg3" else 1
-    steps = max(1, min(args.steps, 5))
-    warm = max(0, min(args.warmup, 1))
-    O, q, cache = cpu_sample(wl, n_req)
-    for _ in range(warm):
-        O.paged_quant_attention(q, cache)
-    ts = []
-    for _ in range(steps):
-        t0 = time.perf_counter()
-        O.paged_quant_attention(q, cache)
-        ts.append(time.perf_counter() - t0)
-    frac = sum((n + 15) // 16 for n in wl.lengths[:n_req]) / sum((n + 15) // 16 for n in wl.lengths)
-    per_call = statistics.median(ts) / frac
-    value = wl.bytes_per_call / per_call / 1e12
-    sample = (f"first {n_req} of {len(wl.lengths)} requests of {wl.name} (their pages only), median of {steps} "
-              f"calls, scaled by page share {frac:.4f}")
-    cores = cpu_threads()
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": args.gpus, "steps": steps,
-        "warmup": warm, "ms_per_step": per_call * 1e3, "us_per_call": per_call * 1e6, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 KV / fp32 accumulate", "data": "synthetic",
-        "config": {"workload": wl.name, "global_batch": len(wl.lengths), "seq_len": max(wl.lengths),
-                   "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    return gather(wl.cache.k_quant), gather(wl.cache.v_quant)
 
 
 def run_ours(args, rank: int, world: int, local_rank: int):
     import torch
-    import torch.distributed as dist
 
     import flashspec_b200 as fs
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    wl = build_workload(args.config, rank, world)
-    q, cache = wl.q, wl.cache
-    splits = wl.num_splits
-    seqshard = args.config == "cfg3"
-    if seqshard:
+    timer = Timer(dev, world)
+    stream = timer.stream
+    cfg = args.config
+    fused = cfg == "cfg0"
+    seqshard = cfg == "cfg3"
+    wl = build_workload(cfg, rank, world)
+    decoder = None
+
+    # ---- the call of one step ----------------------------------------------------------
+    if fused:
+        # cfg0 is 135 MB (about L2 size): rotate over four copies so every call reads HBM
+        copies = [(wl.q, wl.k_quant, wl.v_quant)]
+        for _ in range(3):
+            copies.append((wl.q.clone(), fs.QuantizedTensor(wl.k_quant.values.clone(), wl.k_quant.scale.clone(),
+                                                              wl.k_quant.zero_point.clone(), 16,
+                                                              wl.k_quant.original_shape),
+                           fs.QuantizedTensor(wl.v_quant.values.clone(), wl.v_quant.scale.clone(),
+                                              wl.v_quant.zero_point.clone(), 16, wl.v_quant.original_shape)))
+
+        def step(i):
+            q, kq, vq = copies[i % 4]
+            return fs.fused_dequant_attention_cuda(q, kq, vq)
+    elif seqshard:
         from flashspec_b200.dist import SequenceShardedDecoder
 
         decoder = SequenceShardedDecoder()
-        n_pages = cache.block_table.shape[1]
-        # one CUDA graph per step, unless the step holds an NCCL collective
-        graphable = world == 1 or decoder.transport == "p2p"
-        if graphable:
-            replay, _ = decoder.capture(q, cache, n_pages)
+        n_pages = wl.cache.block_table.shape[1]
+        replay, _ = decoder.capture(wl.q, wl.cache, n_pages)
 
-            def call():
-                replay()
-        else:
-            def call():
-                return decoder(q, cache, n_pages)
+        def step(i):
+            replay()
     else:
-        def call():
-            return fs.paged_quant_attention_cuda(q, cache, num_splits=splits)
+        def step(i):
+            return fs.paged_quant_attention_cuda(wl.q, wl.cache, num_splits=wl.num_splits)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    # warm-up (W steps) and a clock soak of ~1.5 s so nvidia-smi sees the load
+    # ---- warm-up and a clock soak of ~1.5 s so nvidia-smi sees the load ------------------
     sampler = ClockSampler() if rank == 0 else None
-    for _ in range(max(3, args.warmup)):
-        call()
+    for i in range(max(3, args.warmup)):
+        step(i)
     torch.cuda.synchronize()
     if sampler is not None:
         sampler.start()
     t_soak = time.time()
     while not args.no_soak and time.time() - t_soak < 1.5:
-        for _ in range(200):
-            call()
+        for i in range(200):
+            step(i)
         torch.cuda.synchronize()
 
-    # ---- device-resident timed region ------------------------------------------------
-    stream = torch.cuda.current_stream(dev)
-    barrier()
-    t_wall0 = time.time()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for i in range(args.steps):
-        call()
-    end.record(stream)
-    barrier()
+    # ---- device-resident timed region ----------------------------------------------------
+    elapsed_ms = timer.run(step, args.steps)
     t_wall1 = time.time()
-    elapsed_ms = start.elapsed_time(end)
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(t.item())
+    host_us = host_us_per_call(lambda: step(0))
 
-    # per-launch durations for the roofline: the same steps again, each bracketed by
-    # events (kept out of the timed loop above, whose launches they would space apart)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps):
-        evs[i][0].record(stream)
-        call()
-        evs[i][1].record(stream)
-    barrier()
-    launch_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    # ---- end-to-end through the public API with host buffers -----------------------------
+    q = wl.q
+    if fused:
+        host = [q]
 
-    # ---- end-to-end through the public API with host buffers ----------------------------
-    # Every step copies its inputs (q, block table, lengths) from pinned host memory and
-    # reads its output back.  Sequence-sharded runs do it serially on the compute stream.
-    # Otherwise the step's inputs travel as one packed H2D copy on a side stream into one
-    # of two device buffers, and the output comes back on a second side stream, so the
-    # copies of neighbouring steps overlap the decode of this one, as a serving loop
-    # arranges it; the steps are replayed from a CUDA graph of kGraphSteps pipelined steps
-    # so the host's per-step launch work does not pace the GPU.
-    e2e_steps = max(1, min(args.steps, 500))
-    qb = q.numel() * q.element_size()
-    tb = cache.block_table.numel() * 8
-    lb = cache.lengths.numel() * 8
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if seqshard and not graphable:
-        q_host = q.cpu().pin_memory()
-        table_host = cache.block_table.cpu().pin_memory()
-        lengths_host = cache.lengths.cpu().pin_memory()
-        out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-        q_dev, table_dev, lengths_dev = torch.empty_like(q), torch.empty_like(cache.block_table), torch.empty_like(cache.lengths)
-        cache_e2e = fs.PagedKVCache(cache.k_quant, cache.v_quant, table_dev, lengths_dev, cache.block_size,
-                                    cache.max_seq_len)
-
-        def e2e_step(i):
-            q_dev.copy_(q_host, non_blocking=True)
-            table_dev.copy_(table_host, non_blocking=True)
-            lengths_dev.copy_(lengths_host, non_blocking=True)
-            out = decoder(q_dev, cache_e2e, n_pages)
-            out_host.copy_(out, non_blocking=True)
+        def make_run(b, views):
+            kq, vq = copies[b][1], copies[b][2]
+            return lambda: fs.fused_dequant_attention_cuda(views[0], kq, vq)
     else:
-        n_in = qb + tb + lb
-        host_in, dev_in, q_in, caches, outs_host = [], [], [], [], []
-        for b in range(2):
-            h = torch.empty(n_in, dtype=torch.uint8).pin_memory()
-            h[:qb].copy_(q.cpu().contiguous().view(-1).view(torch.uint8))
-            h[qb:qb + tb].copy_(cache.block_table.cpu().contiguous().view(-1).view(torch.uint8))
-            h[qb + tb:].copy_(cache.lengths.cpu().contiguous().view(-1).view(torch.uint8))
-            d = torch.empty(n_in, dtype=torch.uint8, device=dev)
-            host_in.append(h)
-            dev_in.append(d)
-            q_in.append(d[:qb].view(q.dtype).view(q.shape))
-            caches.append(fs.PagedKVCache(cache.k_quant, cache.v_quant,
-                                          d[qb:qb + tb].view(torch.int64).view(cache.block_table.shape),
-                                          d[qb + tb:].view(torch.int64).view(cache.lengths.shape),
-                                          cache.block_size, cache.max_seq_len))
-            outs_host.append(torch.empty(q.shape, dtype=q.dtype).pin_memory())
-        h2d_stream, d2h_stream = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        h2d_done = [torch.cuda.Event() for _ in range(2)]
-        kern_done = [torch.cuda.Event() for _ in range(2)]
-        if seqshard:  # one captured decoder step (decode + exchange) per input buffer
-            graphs = []
-            for b in range(2):
-                dev_in[b].copy_(host_in[b])
-                graphs.append(decoder.capture(q_in[b], caches[b], n_pages))
+        cache = wl.cache
+        host = [q, cache.block_table, cache.lengths]
 
-        def run(b):
-            if seqshard:
-                graphs[b][0]()
-                return graphs[b][1]
-            return fs.paged_quant_attention_cuda(q_in[b], caches[b], num_splits=splits)
+        def make_run(b, views):
+            c = fs.PagedKVCache(cache.k_quant, cache.v_quant, views[1], views[2], cache.block_size,
+                                cache.max_seq_len)
+            if seqshard:  # one captured decoder step (decode + exchange) per input buffer
+                rep, out = decoder.capture(views[0], c, n_pages)
 
-        def pipelined_step(i, cur):
-            b = i % 2
-            if i < 2:  # the first step of each buffer forks from the compute stream
-                h2d_stream.wait_stream(cur)
-            else:
-                h2d_stream.wait_event(kern_done[b])
-            with torch.cuda.stream(h2d_stream):
-                dev_in[b].copy_(host_in[b], non_blocking=True)
-                h2d_done[b].record(h2d_stream)
-            cur.wait_event(h2d_done[b])
-            out = run(b)
-            kern_done[b].record(cur)
-            d2h_stream.wait_event(kern_done[b])
-            with torch.cuda.stream(d2h_stream):
-                outs_host[b].copy_(out, non_blocking=True)
+                def run():
+                    rep()
+                    return out
+                return run
+            return lambda: fs.paged_quant_attention_cuda(views[0], c, num_splits=wl.num_splits)
+    pipe = E2EPipeline(dev, host, make_run, q)
+    kGraphSteps = 10
+    e2e_steps = max(kGraphSteps, min(args.steps, 500) // kGraphSteps * kGraphSteps)
+    if seqshard:  # its steps are graph replays already: issue them eagerly, in pipeline
+        for i in range(4):
+            pipe.step(i, stream)
+        stream.wait_stream(pipe.d2h)
 
-        kGraphSteps = 10
-        for i in range(4):  # eager warm-up: workspaces, tickets, kernel configuration
-            pipelined_step(i, stream)
-        stream.wait_stream(d2h_stream)
-        torch.cuda.synchronize()
-        if seqshard:  # steps are already graph replays: issued eagerly, in pipeline
-            def e2e_step(i):
-                pipelined_step(i + 4, stream)
-                if i == e2e_steps - 1:
-                    stream.wait_stream(d2h_stream)
-        else:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                cap = torch.cuda.current_stream()
-                for i in range(kGraphSteps):
-                    pipelined_step(i, cap)
-                cap.wait_stream(h2d_stream)
-                cap.wait_stream(d2h_stream)
-            e2e_steps = max(kGraphSteps, e2e_steps // kGraphSteps * kGraphSteps)
+        def e2e(i):
+            pipe.step(i + 4, stream)
+            if i == e2e_steps - 1:
+                stream.wait_stream(pipe.d2h)
+    else:
+        replay_e2e = pipe.graph(kGraphSteps)
 
-            def e2e_step(i):
-                if i % kGraphSteps == 0:
-                    graph.replay()
-
-    for i in range(3):
-        e2e_step(i if (seqshard and not graphable) else 0)
-    barrier()
-    e0.record(stream)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1)
-    te = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_ms = float(te.item())
-    h2d = qb + tb + lb
-    d2h = qb
+        def e2e(i):
+            if i % kGraphSteps == 0:
+                replay_e2e()
+    for i in range(3 * kGraphSteps):
+        e2e(i)
+    e2e_ms = timer.run(e2e, e2e_steps)
     if sampler is not None:
         sampler.stop()
+    if decoder is not None:
+        decoder.close()  # raises if any exchange timed out
+
+    # ---- sub-objects ---------------------------------------------------------------------
+    extras = {}
+    if not args.no_extras and cfg == "cfg1":
+        extras["seqshard"] = seqshard_sub(args, rank, world, dev, timer)
+        if world == 1:
+            extras["paged_vs_contiguous"] = paged_vs_contiguous(args, wl, timer, elapsed_ms / args.steps)
+    read_gbs = read_probe_gbs(dev) if (rank == 0 and not args.no_extras) else None
     if rank != 0:
         return
 
+    # ---- the JSON line -------------------------------------------------------------------
     peak, peak_kind = measured_peaks()
-    # bytes one rank's decode moves (cfg3: its own page window + q/out + table), per step
+    per_call_ms = elapsed_ms / args.steps
+    # bytes one rank's decode moves per step (cfg3: its own page window + q/out + table)
     launch_bytes = wl.bytes_per_call // world if seqshard else wl.bytes_per_call
-    achieved_gbs = launch_bytes / (launch_ms * 1e-3) / 1e9
+    achieved = launch_bytes / (per_call_ms * 1e-3) / 1e9
     calls_bytes = wl.bytes_per_call * (1 if seqshard else world)  # cfg3: one call spans all ranks
-    total_bytes = calls_bytes * args.steps
-    value = total_bytes / (elapsed_ms * 1e-3) / 1e12
+    value = calls_bytes * args.steps / (elapsed_ms * 1e-3) / 1e12
     e2e_value = calls_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e12
-    clocks = sampler.summary(t_soak, t_wall1) if sampler is not None else {}
+    batch = int(wl.q.shape[0]) * (1 if seqshard else world)
+    seq_len = int(wl.k_quant.original_shape[2]) if fused else max(wl.lengths)
+    traffic, traffic_src = traffic_per_launch(cfg)
+    if seqshard and world > 1:
+        traffic = None  # the committed capture is of the one-rank launch
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic, "traffic_source": traffic_src,
+                "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                "kernel_us": per_call_ms * 1e3,
+                "kernel_us_source": "mean launch time over the timed region (CUDA events on the launching stream)"
+                                    + ("; the step also runs the exchange kernel" if seqshard and world > 1 else ""),
+                "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS}
+    if read_gbs is not None:
+        roofline.update({"read_peak_gbs": read_gbs, "frac_of_read_peak": achieved / read_gbs,
+                         "read_peak_kind": "measured in this run: fs_read_bandwidth_probe over 4 GiB, best of 5"})
+    api = ("flashspec_b200.fused_dequant_attention_cuda" if fused else
+           "flashspec_b200 sequence-sharded decoder (decode + exchange captured per step)" if seqshard else
+           "flashspec_b200.paged_quant_attention_cuda")
     line = {
         "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(3, args.warmup), "ms_per_step": elapsed_ms / args.steps,
-        "us_per_call": elapsed_ms / args.steps * 1e3, "higher_is_better": True,
+        "warmup": max(3, args.warmup), "ms_per_step": per_call_ms, "us_per_call": per_call_ms * 1e3,
+        "tokens_per_s": batch / (per_call_ms * 1e-3), "higher_is_better": True,
         "scaling": "strong" if seqshard else "weak",
         "vs_baseline": None, "dtype": "int8 KV, fp16 q/out, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": wl.name, "global_batch": len(wl.lengths) * (1 if seqshard else world),
-                   "seq_len": max(wl.lengths), "q_heads": wl.q_heads, "kv_heads": wl.kv_heads, "page": 16,
-                   "parallelism": (f"sequence-shard x{world} ({'peer-memory exchange' if decoder.transport == 'p2p' else 'NCCL all-gather'} of O/LSE + merge)" if seqshard
+        "config": {"workload": wl.name, "global_batch": batch, "seq_len": seq_len,
+                   "q_heads": wl.q_heads if not fused else 32, "kv_heads": wl.kv_heads if not fused else 32,
+                   "page": 16,
+                   "parallelism": (f"sequence-shard x{world} (peer-memory exchange of O/LSE + merge)" if seqshard
                                    else f"request-shard x{world}" if world > 1 else "single"),
-                   "l2": "inputs larger than L2 (no flush)", "bytes_per_call_per_gpu": wl.bytes_per_call},
-        "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
-                     "frac": achieved_gbs / peak, "traffic": traffic_per_launch(args.config),
-                     "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
-                     "kernel_us": launch_ms * 1e3},
-        "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "us_per_call": e2e_ms / e2e_steps * 1e3,
-                "api": ("flashspec_b200 sequence-sharded decoder, q/table/lengths copied from pinned host and "
-                        "the output read back serially every step" if (seqshard and not graphable) else
-                        "flashspec_b200 sequence-sharded decoder, each step a CUDA-graph replay of decode + exchange; "
-                        "every step one packed H2D of q/table/lengths from pinned host (side stream, double-buffered) "
-                        "and its output read back (second side stream), overlapping the neighbouring steps" if seqshard else
-                        "flashspec_b200.paged_quant_attention_cuda replayed from a CUDA graph of 10 steps; every "
-                        "step one packed H2D of q/table/lengths from pinned host (side stream, double-buffered) "
-                        "and its output read back (second side stream), overlapping the neighbouring steps' decode")},
+                   "l2": ("four rotated input copies (135 MB each, > L2 together)" if fused
+                          else "inputs larger than L2 (no flush)"),
+                   "bytes_per_call_per_gpu": launch_bytes},
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": pipe.h2d_bytes,
+                "d2h_bytes_per_step": pipe.d2h_bytes, "us_per_call": e2e_ms / e2e_steps * 1e3,
+                "api": api + ("; each step a graph replay, its inputs copied H2D from pinned host on a side stream "
+                              "(double-buffered) and its output read back on a second side stream" if seqshard else
+                              " replayed from a CUDA graph of 10 steps; every step one packed H2D of its inputs from "
+                              "pinned host (side stream, double-buffered) and its output read back (second side "
+                              "stream), overlapping the neighbouring steps' decode")},
+        "host_us_per_call": host_us,
         "gpu_launches": args.steps * (2 if seqshard else 1),
-        "clocks": clocks,
+        "clocks": sampler.summary(t_soak, t_wall1) if sampler is not None else {},
     }
-    if world == 1 and not args.no_cpu_baseline and not seqshard:
-        n_req = 2 if args.config != "cfg3" else 1
-        full_s, ts = time_cpu_baseline(wl, n_req, reps=3)
+    line.update(extras)
+    if world == 1 and not args.no_cpu_baseline and cfg in ("cfg0", "cfg1", "cfg2"):
+        _, ts, per_call, cores, _ = cpu_reference_line(cfg, 1, 3, budget_s=30.0)
         line["cpu_baseline"] = {
-            "value": wl.bytes_per_call / full_s / 1e12, "unit": "TB/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"first {n_req} requests of {wl.name} (their pages), median of 3 calls, scaled by page share",
-            "us_per_call": full_s * 1e6,
+            "value": wl.bytes_per_call / per_call / 1e12, "unit": "TB/s", "cores": cores, "kind": "port",
+            "sample": f"whole calls of {wl.name} on host-built inputs: 1 warm-up + {len(ts)} timed",
+            "us_per_call": per_call * 1e6, "os_cpu_count": os.cpu_count(),
+            "impl": "oracle/torch_reference.py (reference CPU backends restated in torch)",
         }
     print(json.dumps(line), flush=True)
+
+
+def paged_vs_contiguous(args, wl, timer, paged_ms: float):
+    """The cfg1 KV in the contiguous layout through the fused entry point, same run.  The
+    two are timed alternately (five rounds each, median), both with the same lengths,
+    so clock drift under the power cap does not favour either."""
+    import torch
+
+    import flashspec_b200 as fs
+
+    kq, vq = contiguous_copy(wl)
+    q, lengths = wl.q, wl.cache.lengths
+
+    def contiguous(i):
+        fs.fused_dequant_attention_cuda(q, kq, vq, lengths)
+
+    def paged(i):
+        fs.paged_quant_attention_cuda(q, wl.cache)
+
+    for i in range(max(3, args.warmup)):
+        contiguous(i)
+    n = max(50, min(args.steps, 500))
+    tc, tp = [], []
+    for _ in range(5):
+        tp.append(timer.run(paged, n) / n)
+        tc.append(timer.run(contiguous, n) / n)
+    mp, mc = statistics.median(tp), statistics.median(tc)
+    out_c = fs.fused_dequant_attention_cuda(q, kq, vq, lengths)
+    out_p = fs.paged_quant_attention_cuda(q, wl.cache)
+    same = bool(torch.equal(out_c, out_p))
+    del kq, vq
+    torch.cuda.empty_cache()
+    return {"paged_us": mp * 1e3, "contiguous_us": mc * 1e3, "paged_over_contiguous": mp / mc,
+            "outputs_bit_identical": same, "rounds": 5, "calls_per_round": n,
+            "note": "same int8 bytes and lengths; contiguous = values [B, H, nblk, 16, D] through fs_fused_decode; "
+                    "alternating rounds, medians"}
+
+
+def seqshard_sub(args, rank: int, world: int, dev, timer):
+    """cfg3 (B2, 64q/8kv, 131072 tokens) split by page windows over the N ranks and merged
+    through the peer-memory exchange; rank 0 checks its merged output against a
+    single-GPU decode of the whole sequence rebuilt from every rank's window."""
+    import torch
+
+    import flashspec_b200 as fs
+    from flashspec_b200 import configs
+    from flashspec_b200.dist import SequenceShardedDecoder, page_window
+
+    wl = configs.cfg3_shard(rank, world)
+    n_pages = int(wl.cache.block_table.shape[1])
+    dec = SequenceShardedDecoder()
+    replay, out = dec.capture(wl.q, wl.cache, n_pages)
+    for _ in range(max(3, args.warmup)):
+        replay()
+    steps = max(20, min(args.steps, 2000))
+    ms = timer.run(lambda i: replay(), steps) / steps
+    torch.cuda.synchronize()
+    dec.close()  # raises if an exchange timed out
+    res = {"workload": wl.name, "n_gpus": world, "us_per_call": ms * 1e3,
+           "value": wl.bytes_per_call / (ms * 1e-3) / 1e12, "unit": "TB/s (whole call, all ranks)",
+           "bytes_per_call": wl.bytes_per_call, "steps": steps,
+           "parallelism": f"sequence-shard x{world}, peer-memory exchange" if world > 1 else "one GPU (decode + merge)"}
+    if rank == 0:
+        # the whole sequence on this GPU: every rank's window pool, concatenated
+        pools_k, pools_v, table = [], [], torch.full_like(wl.cache.block_table, -1)
+        off = 0
+        for r in range(world):
+            w = wl if r == 0 else configs.cfg3_shard(r, world)
+            lo, hi = page_window(n_pages, r, world)
+            t = w.cache.block_table[:, lo:hi]
+            table[:, lo:hi] = torch.where(t >= 0, t + off, t)
+            pools_k.append(w.cache.k_quant)
+            pools_v.append(w.cache.v_quant)
+            off += int(w.cache.k_quant.values.shape[0])
+
+        def cat(parts):
+            return fs.QuantizedTensor(torch.cat([p.values for p in parts]), torch.cat([p.scale for p in parts]),
+                                      torch.cat([p.zero_point for p in parts]), 16,
+                                      (off,) + tuple(parts[0].original_shape[1:]))
+
+        full = fs.PagedKVCache(cat(pools_k), cat(pools_v), table, wl.cache.lengths, 16, wl.cache.max_seq_len)
+        ref = fs.paged_quant_attention_cuda(wl.q, full).float()
+        err = (out.float() - ref).abs()
+        ok = bool(torch.all(err <= 2e-3 + 1e-2 * ref.abs()))
+        res["parity_vs_single_gpu_full_decode"] = {"max_abs_err": float(err.max()), "within_2e-3_abs_1e-2_rel": ok}
+    return res
 
 
 def run_serving(args, rank: int, world: int, local_rank: int):
@@ -507,13 +732,14 @@ def run_serving(args, rank: int, world: int, local_rank: int):
     res = run(cfg, device=f"cuda:{local_rank}")
     if rank != 0:
         return
-    step_s = res["step_ms_mean"] * 1e-3
     moved = res["attention_bytes"] + res["append_bytes"]
     peak, peak_kind = measured_peaks()
     att_gbs = res["attention_bytes"] / (res["attention_ms_total"] * 1e-3) / 1e9
+    step_total_s = res["step_ms_mean"] * res["steps_measured"] * 1e-3
     line = {
-        "metric": METRIC, "value": moved / (sum([res["step_ms_mean"]] * args.steps) * 1e-3) / 1e12 * world,
+        "metric": METRIC, "value": moved / step_total_s / 1e12 * world,
         "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": 0, "ms_per_step": res["step_ms_mean"],
+        "tokens_per_s": res["tokens_per_s_device"] * world,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 KV, fp16 q/out/tokens, fp32 accumulate", "data": "synthetic",
         "config": {"workload": "cfg4_serving_loop", "parallelism": f"request-shard x{world}" if world > 1 else "single",
@@ -521,7 +747,7 @@ def run_serving(args, rank: int, world: int, local_rank: int):
         "roofline": {"bound": "hbm", "achieved": att_gbs, "peak": peak, "unit": "GB/s", "frac": att_gbs / peak,
                      "traffic": None, "peak_kind": f"{peak_kind} copy bandwidth", "kernel": "attention launches"},
         "serving": res,
-        "gpu_launches": None,
+        "gpu_launches": res.get("gpu_launches"),
     }
     print(json.dumps(line), flush=True)
 
@@ -532,21 +758,18 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        if args.config == "cfg4":
-            print(json.dumps({"impl": "reference", "unavailable": "cfg4 reference arm not implemented"}))
-            return
         run_reference(args, rank, world)
         return
     if args.config == "cfg4":
         run_serving(args, rank, world, local_rank)
         return
     if world > 1:
+        import datetime
+
         import torch
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
-        import datetime
-
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
                                 timeout=datetime.timedelta(seconds=120))
     try:

@@ -151,6 +151,8 @@ SIGNATURES = {
     "fs_exchange_destroy": (C.c_int, [C.c_void_p]),
     "fs_exchange_merge": (C.c_int, [C.POINTER(FsExchangeArgs), C.c_void_p]),
     "fs_page_update": (C.c_int, [C.POINTER(FsPageUpdateArgs), C.c_void_p]),
+    "fs_read_bandwidth_probe": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int32, C.POINTER(C.c_int32),
+                                          C.c_void_p]),
     "fs_dequantize_pages": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                       C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
 }

@@ -13,15 +13,20 @@
 // Protocol: every value travels as one naturally aligned 8-byte word, (value bits,
 // call epoch) -- single-copy atomic -- so a receiver knows a word has arrived when its
 // tag equals the current epoch, without fences or separate flags.  Buffer layout
-// (bytes): [0, 256) per-CTA call counters (epoch of CTA c's last completed call); then
-// two epoch parities x kXMaxRanks slots of slot_floats words (O [rows][D], then LSE
-// [rows]).  Parity: a peer may begin its next call as soon as it has this rank's words,
+// (bytes): [0, 256) per-CTA call counters (epoch of CTA c's last completed call);
+// [256, 264) the slot size the buffer was created with (read back by fs_exchange_open,
+// so fs_exchange_merge can refuse a slot size that would store past a peer's buffer);
+// from 512 two epoch parities x kXMaxRanks slots of slot_floats words (O [rows][D],
+// then LSE [rows]).  Parity: a peer may begin its next call as soon as it has this rank's words,
 // so its next words land in the other parity while this rank still reads the current
 // one; it cannot get two calls ahead, as that needs this rank's words of the next call.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
+
+#include <mutex>
+#include <unordered_map>
 
 #include "../../include/flashspec_b200.h"
 #include "common.h"
@@ -32,9 +37,34 @@ namespace fsb {
 constexpr int kXMaxRanks = FS_EXCHANGE_MAX_RANKS;
 constexpr int kXMaxCtas = 64;
 constexpr int kXThreads = 256;
-constexpr size_t kXCtrlBytes = 256;  // kXMaxCtas 32-bit call counters
-constexpr size_t kXDataOffset = kXCtrlBytes;
-static_assert(kXMaxCtas * 4 <= kXCtrlBytes, "call counters");
+constexpr size_t kXCountersBytes = 256;  // kXMaxCtas 32-bit call counters
+constexpr size_t kXSlotSizeOffset = kXCountersBytes;  // int64 slot_floats of the buffer
+constexpr size_t kXDataOffset = 512;
+static_assert(kXMaxCtas * 4 <= kXCountersBytes, "call counters");
+
+// Slot size of every exchange buffer this process created or mapped, by address.
+static std::mutex g_xbuf_mu;
+static std::unordered_map<const void*, int64_t> g_xbuf_slots;
+
+static void remember_buffer(const void* p, int64_t slot_floats) {
+  std::lock_guard<std::mutex> lock(g_xbuf_mu);
+  g_xbuf_slots[p] = slot_floats;
+}
+
+static void forget_buffer(const void* p) {
+  std::lock_guard<std::mutex> lock(g_xbuf_mu);
+  g_xbuf_slots.erase(p);
+}
+
+// true when every buffer of the call is known here and was made for this slot size
+static bool buffers_match(const FsExchangeArgs* a) {
+  std::lock_guard<std::mutex> lock(g_xbuf_mu);
+  for (int p = 0; p < a->world; ++p) {
+    const auto it = g_xbuf_slots.find(a->bufs[p]);
+    if (it == g_xbuf_slots.end() || it->second != a->slot_floats) return false;
+  }
+  return true;
+}
 
 __device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t tag) {
   const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
@@ -80,10 +110,12 @@ __global__ void __launch_bounds__(kXThreads) exchange_merge_kernel(const FsExcha
   }
   __syncthreads();
   // 2. merge the slice as the words arrive: out = sum_p w_p O_p / sum_p w_p,
-  //    w_p = exp(lse_p - max lse) (triton_fused.py:446-503 on one partial per rank)
+  //    w_p = exp(lse_p - max lse) (triton_fused.py:446-503 on one partial per rank).
+  //    Once a wait has run out, this thread waits no more and writes NaN for the rest
+  //    of its elements, so a timed-out call never leaves plausible-looking output.
   const uint64_t* data = reinterpret_cast<const uint64_t*>(own + parity_off);
   bool ok = true;
-  for (int64_t i = r0 * D + tid; i < r1 * D && ok; i += kXThreads) {
+  for (int64_t i = r0 * D + tid; i < r1 * D; i += kXThreads) {
     const int64_t row = i / D;
     float lse[kXMaxRanks], o[kXMaxRanks];
     float M = -INFINITY;
@@ -97,9 +129,8 @@ __global__ void __launch_bounds__(kXThreads) exchange_merge_kernel(const FsExcha
         M = fmaxf(M, lse[p]);
       }
     }
-    if (!ok) break;
     float W = 0.f, O = 0.f;
-    if (M != -INFINITY)
+    if (ok && M != -INFINITY)
 #pragma unroll
       for (int p = 0; p < kXMaxRanks; ++p)
         if (p < a.world) {
@@ -107,7 +138,7 @@ __global__ void __launch_bounds__(kXThreads) exchange_merge_kernel(const FsExcha
           W += w;
           O += w * o[p];
         }
-    const float v = W > 0.f ? O / W : 0.f;
+    const float v = !ok ? __int_as_float(0x7fc00000) : W > 0.f ? O / W : 0.f;
     if (a.out_dtype == FS_F16)
       static_cast<__half*>(a.out)[i] = __float2half_rn(v);
     else
@@ -137,10 +168,16 @@ int fs_exchange_create(int64_t slot_floats, void** buf, void* ipc_handle) {
     return fail_cuda("cudaMemset of the exchange buffer", e);
   }
   cudaIpcMemHandle_t h;
+  if ((e = cudaMemcpy(static_cast<uint8_t*>(p) + kXSlotSizeOffset, &slot_floats, sizeof(slot_floats),
+                      cudaMemcpyHostToDevice)) != cudaSuccess) {
+    cudaFree(p);
+    return fail_cuda("cudaMemcpy of the exchange buffer's slot size", e);
+  }
   if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
     cudaFree(p);
     return fail_cuda("cudaIpcGetMemHandle of the exchange buffer", e);
   }
+  remember_buffer(p, slot_floats);
   static_assert(sizeof(h) == FS_EXCHANGE_HANDLE_BYTES, "IPC handle size");
   memcpy(ipc_handle, &h, sizeof(h));
   *buf = p;
@@ -151,16 +188,28 @@ int fs_exchange_open(const void* ipc_handle, void** peer_buf) {
   if (ipc_handle == nullptr || peer_buf == nullptr) return FS_ERR_INVALID_ARGUMENT;
   cudaIpcMemHandle_t h;
   memcpy(&h, ipc_handle, sizeof(h));
-  const cudaError_t e = cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess);
-  return e == cudaSuccess ? FS_OK : fsb::fail_cuda("cudaIpcOpenMemHandle of a peer exchange buffer", e);
+  cudaError_t e = cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fsb::fail_cuda("cudaIpcOpenMemHandle of a peer exchange buffer", e);
+  int64_t slot_floats = 0;
+  e = cudaMemcpy(&slot_floats, static_cast<const uint8_t*>(*peer_buf) + fsb::kXSlotSizeOffset, sizeof(slot_floats),
+                 cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    cudaIpcCloseMemHandle(*peer_buf);
+    *peer_buf = nullptr;
+    return fsb::fail_cuda("cudaMemcpy of a peer exchange buffer's slot size", e);
+  }
+  fsb::remember_buffer(*peer_buf, slot_floats);
+  return FS_OK;
 }
 
 int fs_exchange_close(void* peer_buf) {
+  fsb::forget_buffer(peer_buf);
   const cudaError_t e = cudaIpcCloseMemHandle(peer_buf);
   return e == cudaSuccess ? FS_OK : fsb::fail_cuda("cudaIpcCloseMemHandle", e);
 }
 
 int fs_exchange_destroy(void* buf) {
+  fsb::forget_buffer(buf);
   const cudaError_t e = cudaFree(buf);
   return e == cudaSuccess ? FS_OK : fsb::fail_cuda("cudaFree of the exchange buffer", e);
 }
@@ -174,6 +223,9 @@ int fs_exchange_merge(const FsExchangeArgs* a, void* stream) {
   if (a->out_dtype != FS_F16 && a->out_dtype != FS_F32) return FS_ERR_UNSUPPORTED;
   for (int p = 0; p < a->world; ++p)
     if (a->bufs[p] == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  // every buffer must come from fs_exchange_create / fs_exchange_open with this slot size:
+  // a larger one would make the kernel store past the end of a peer's buffer
+  if (!buffers_match(a)) return FS_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(a->o_mine) & 15) return FS_ERR_ALIGNMENT;
   // slices of whole rows whose O part is a multiple of 4 floats
   int rows_per_cta = (int)((a->rows + kXMaxCtas - 1) / kXMaxCtas);

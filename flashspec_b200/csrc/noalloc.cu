@@ -17,8 +17,12 @@
 //
 // All calls share the one array and each call leaves its last contents there:
 // calls that can overlap on the GPU (different streams, no ordering) race on it and
-// must be serialised by the caller.  The counters are cleared (cudaMemsetAsync on the
-// call's stream, not an allocation) before every launch.
+// must be serialised by the caller.  Whenever the plan merges partial results (the
+// split kernel with more than one split, or the balanced kernel, which merges the
+// pieces of a (request, kv head) pair that several warps share) the counters of the
+// call's pairs are cleared (cudaMemsetAsync on the call's stream, not an allocation)
+// before the launch, so a call that an earlier timeout left with non-zero counters
+// still merges correctly.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -89,7 +93,9 @@ extern "C" int fs_paged_decode_noalloc(const FsDecodeArgs* args, void* stream) {
   a.ticket_count = (int64_t)(kTicketBytes / 4);
   a.workspace = scratch + kTicketBytes;
   a.workspace_bytes = kPartialBytes;
-  if (splits > 1) {
+  // fs_decode_workspace_size reports 0 splits for the balanced kernel and 1 for a
+  // split kernel that writes the output directly; every other plan uses the counters.
+  if (splits != 1) {
     const cudaError_t e =
         cudaMemsetAsync(a.tickets, 0, (size_t)a.batch * a.kv_heads * 4, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail_cuda("cudaMemsetAsync of the no-alloc tickets", e);

@@ -1,6 +1,6 @@
 """Multi-GPU decode: one process per GPU, torch.distributed for the plumbing.
 
-Two strategies (the reference has no multi-GPU path; SURVEY of the hot path):
+Two strategies (the reference has no multi-GPU path):
 
 * request x kv-head sharding (configs 0, 1, 2, 4): every rank owns whole requests
   and runs the single-GPU kernel on them.  No communication; see ``request_shard``.
@@ -121,6 +121,18 @@ class PeerExchange:
         _lib.check(self._lib.fs_exchange_merge(C.byref(a), stream_of(self.device)), "fs_exchange_merge")
         return out
 
+    def check(self) -> None:
+        """Raise if any merge so far gave up waiting for a peer (FS_DEV_TIMEOUT in the
+        status word).  Waits for this device's queued work.  A timed-out call wrote NaN
+        to the rows it could not merge, and the ranks' call counters may now disagree,
+        so the group must close its exchange (collectively) and create a new one."""
+        from . import _lib
+
+        st = int(self.status.item())
+        if st & _lib.FS_DEV_TIMEOUT:
+            raise RuntimeError(f"peer exchange on rank {self.rank} timed out waiting for a peer (status {st}); "
+                               "close the decoder's exchange on every rank and recreate it")
+
     def close_peers(self) -> None:
         """Unmap the peers' buffers (this rank stops addressing them)."""
         with torch.cuda.device(self.device):
@@ -158,8 +170,12 @@ class SequenceShardedDecoder:
 
     def __init__(self, group: Optional[dist.ProcessGroup] = None,
                  partial_fn: Optional[Callable] = None, merge_fn: Optional[Callable] = None,
-                 transport: Optional[str] = None, timeout_ms: float = 2000.0):
+                 transport: Optional[str] = None, timeout_ms: float = 2000.0, check_every: int = 0):
         self.group = group
+        # check_every > 0: read the exchange status word every that many calls (a host
+        # synchronisation); 0 leaves it to check() and close()
+        self.check_every = int(check_every)
+        self._calls = 0
         self.partial_fn = partial_fn
         self.merge_fn = merge_fn
         # multi-rank CUDA steps: "p2p" (peer-memory exchange kernel) or "nccl" (all-gather)
@@ -220,7 +236,11 @@ class SequenceShardedDecoder:
             xch = self._xch.get(xkey)
             if xch is None:
                 xch = self._xch[xkey] = PeerExchange(self.group, q.device, slot, self.timeout_ns)
-            return xch.merge(o, lse, torch.empty(q.shape, dtype=out_dtype, device=q.device))
+            out = xch.merge(o, lse, torch.empty(q.shape, dtype=out_dtype, device=q.device))
+            self._calls += 1
+            if self.check_every > 0 and self._calls % self.check_every == 0:
+                xch.check()
+            return out
         if self.world > 1:  # out of place: the send buffer is not a view of the receive buffer
             dist.all_gather_into_tensor(gather.view(-1), mine, group=self.group)
         else:
@@ -232,11 +252,25 @@ class SequenceShardedDecoder:
                                                  code, stream_of(q.device)), "fs_merge_partials")
         return out
 
-    def close(self) -> None:
+    def check(self) -> None:
+        """Raise RuntimeError if an exchange of this decoder has timed out (see
+        ``PeerExchange.check``); synchronises with the device."""
+        for x in self._xch.values():
+            x.check()
+
+    def close(self, check: bool = True) -> None:
         """Release the peer-exchange buffers (collectively: every rank calls it, after its
-        last step has finished on the GPU; further calls set them up again)."""
+        last step has finished on the GPU; further calls set them up again).  With
+        ``check`` the status words are read first and a timeout is raised after the
+        buffers are released."""
+        failure = None
         if self._xch:
             torch.cuda.synchronize()
+            if check:
+                try:
+                    self.check()
+                except RuntimeError as e:
+                    failure = e
             multi = dist.is_initialized() and self.world > 1
             if multi:
                 dist.barrier(group=self.group)  # every rank's last exchange has finished
@@ -247,6 +281,8 @@ class SequenceShardedDecoder:
             for x in self._xch.values():
                 x.destroy()
             self._xch.clear()
+        if failure is not None:
+            raise failure
 
     def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16):
         """Record the decode step of a single-rank group (partial kernel + merge) as a CUDA

@@ -95,6 +95,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
     t_attn = t_append = t_prefill = 0.0
     attn_bytes = append_bytes = 0
     tokens = finished = admitted = 0
+    launches = 0  # this library's kernels: one page update per prefill, per append, one decode per step
     ev = lambda: torch.cuda.Event(enable_timing=True)
     step_times = []
     marks = []
@@ -115,6 +116,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
             k = torch.randn((1, cfg.heads, r.prompt, cfg.head_dim), generator=gen, device=device, dtype=torch.float16)
             v = torch.randn((1, cfg.heads, r.prompt, cfg.head_dim), generator=gen, device=device, dtype=torch.float16)
             alloc.add_request(r.rid, k, v)
+            launches += 1 if r.prompt > 0 else 0
             if recorder is not None:
                 recorder.append(("add", r.rid, k.cpu().numpy(), v.cpu().numpy()))
             live[r.rid] = r
@@ -148,6 +150,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
         t1.record()
         attn_bytes += algorithmic_bytes(b, cfg.heads, cfg.heads, lens, table_cols=int(cache.block_table.shape[1]))
         tokens += b
+        launches += 2
         if recorder is not None:
             recorder.append(("attn", list(ids), q.cpu().numpy(), out.cpu().numpy()))
         # 4. release finished requests
@@ -189,6 +192,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
             "append_tbps": append_bytes / (t_append * 1e-3) / 1e12 if t_append else None,
             "attention_bytes": attn_bytes, "append_bytes": append_bytes,
             "tokens_per_s_device": tokens / (sum(step_times) * 1e-3),
+            "steps_measured": len(step_times), "gpu_launches": launches,
         })
     return res
 

@@ -149,10 +149,14 @@ int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_pa
  * fs_exchange_merge, per step, on every rank (the same number of calls on each): one
  * kernel stores this rank's partial rows into every rank's buffer (plain peer stores
  * over NVLink) and waits for every rank's rows -- up to timeout_ns, after which it sets
- * FS_DEV_TIMEOUT in device_status and leaves the rest of `out` unwritten -- and writes
- * the merged rows [rows, head_dim] to `out` (FS_F16 or FS_F32).  No host sync and
- * no collective library call, so a step that uses it can be recorded in a CUDA graph.
- * After a timeout the buffers' call counters may disagree: recreate them. */
+ * FS_DEV_TIMEOUT in device_status and writes NaN to the rows it could not merge -- and
+ * writes the merged rows [rows, head_dim] to `out` (FS_F16 or FS_F32).  No host sync
+ * and no collective library call, so a step that uses it can be recorded in a CUDA
+ * graph.  Every buffer in bufs[] must come from fs_exchange_create / fs_exchange_open of
+ * this process with the same slot_floats, else FS_ERR_INVALID_ARGUMENT (a larger slot
+ * would store past the end of a peer's buffer).  After a timeout the ranks' call
+ * counters may disagree: every rank must close and destroy its buffers and create new
+ * ones. */
 #define FS_EXCHANGE_MAX_RANKS 8
 #define FS_EXCHANGE_HANDLE_BYTES 64
 typedef struct FsExchangeArgs {
@@ -227,6 +231,14 @@ int fs_page_update(const FsPageUpdateArgs* args, void* stream);
 int fs_dequantize_pages(const int8_t* values, const float* scale, const int16_t* zero_point,
                         const int64_t* pages, int64_t n_pages_listed, int64_t num_pages, int32_t heads,
                         int32_t block_size, int32_t head_dim, float* out, void* stream);
+
+/* Measurement aid, no counterpart in the reference: streams `bytes` (a multiple of 16,
+ * 16-byte aligned buffer) through a read-only kernel and stores one 32-bit XOR per CTA
+ * into sink[0 .. *ctas_used) (sink_count entries at least as many as the CTAs used, at
+ * most resident CTAs).  Time it with events to get the GPU's read-only HBM bandwidth,
+ * the denominator for kernels that mostly read (the decode kernels). */
+int fs_read_bandwidth_probe(const void* buf, size_t bytes, uint32_t* sink, int32_t sink_count, int32_t* ctas_used,
+                            void* stream);
 
 #ifdef __cplusplus
 }

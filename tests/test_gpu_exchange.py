@@ -2,10 +2,10 @@
 
 On one GPU: a one-rank exchange must give exactly fs_merge_partials' result, call
 after call, and a two-rank exchange whose peer never arrives must give up within its
-time limit and say so in the status word (the GPU stays usable).  With two GPUs: two
-ranks (child processes, gloo for the handle exchange) decode their page windows and
-merge through the exchange, eagerly and as CUDA-graph replays, and must match the
-single-GPU decode."""
+time limit, say so in the status word and write NaN (the GPU stays usable).  With two
+GPUs: two ranks (child processes, gloo for the handle exchange) decode their page
+windows and merge through the exchange, eagerly and as CUDA-graph replays, and must
+match the CPU oracle on the whole sequence."""
 
 from __future__ import annotations
 
@@ -82,8 +82,10 @@ def test_one_rank_exchange_equals_merge_partials_on_consecutive_calls():
 
 
 def test_missing_peer_times_out_and_reports():
-    """Rank 0 of a two-rank exchange whose rank 1 never runs: the kernel waits on a flag
-    nothing sets, gives up after 20 ms, sets FS_DEV_TIMEOUT, and the device stays usable."""
+    """Rank 0 of a two-rank exchange whose rank 1 never runs: the kernel waits for the
+    peer's tagged words, which nothing writes, gives up after 20 ms, sets FS_DEV_TIMEOUT
+    and writes NaN rather than a partial merge; a second call on the same buffers does
+    the same (its epoch has moved on, the peer's has not), and the device stays usable."""
     _need_gpu()
     from flashspec_b200 import _lib
 
@@ -99,17 +101,39 @@ def test_missing_peer_times_out_and_reports():
         a.bufs[0], a.bufs[1] = mine, silent_peer
         a.slot_floats, a.rows, a.head_dim = slot, rows, d
         a.o_mine, a.lse_mine = o.data_ptr(), lse.data_ptr()
-        out = torch.empty_like(wl.q)
-        a.out, a.out_dtype = out.data_ptr(), _lib.FS_F16
+        a.out_dtype = _lib.FS_F16
         a.timeout_ns, a.device_status = 20 * 10**6, status.data_ptr()
-        assert lib.fs_exchange_merge(C.byref(a), torch.cuda.current_stream().cuda_stream) == 0
-        torch.cuda.synchronize()
-        assert int(status.item()) & _lib.FS_DEV_TIMEOUT
+        for _ in range(2):
+            status.zero_()
+            out = torch.zeros_like(wl.q)
+            a.out = out.data_ptr()
+            assert lib.fs_exchange_merge(C.byref(a), torch.cuda.current_stream().cuda_stream) == 0
+            torch.cuda.synchronize()
+            assert int(status.item()) & _lib.FS_DEV_TIMEOUT
+            assert bool(torch.isnan(out).all()), "a timed-out merge must not return values"
         assert float(torch.ones(4, device="cuda").sum()) == 4.0  # context still usable
+        # a slot size other than the buffers were created with is refused before launch
+        a.slot_floats = slot + 64
+        assert lib.fs_exchange_merge(C.byref(a), torch.cuda.current_stream().cuda_stream) == 1
     finally:
         torch.cuda.synchronize()
         lib.fs_exchange_destroy(mine)
         lib.fs_exchange_destroy(silent_peer)
+
+
+def test_decoder_check_raises_after_a_timeout():
+    """PeerExchange.check() turns FS_DEV_TIMEOUT into an exception on the host."""
+    _need_gpu()
+    from flashspec_b200 import _lib
+    from flashspec_b200.dist import PeerExchange
+
+    x = PeerExchange.__new__(PeerExchange)
+    x.rank = 0
+    x.status = torch.tensor([_lib.FS_DEV_TIMEOUT], dtype=torch.int32, device="cuda")
+    with pytest.raises(RuntimeError, match="timed out"):
+        x.check()
+    x.status.zero_()
+    x.check()
 
 
 def _free_port() -> int:
@@ -122,16 +146,25 @@ def _rank_main(rank, world, port, out_dir):
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
 
-    import flashspec_b200 as fs
     from flashspec_b200 import configs
     from flashspec_b200.dist import SequenceShardedDecoder
 
     torch.cuda.set_device(rank)
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import flashspec_oracle as O
+
     wl = configs.paged_workload("xch2", 2, 16, 2, [3000, 1301], seed=5, device=f"cuda:{rank}")
     n_pages = int(wl.cache.block_table.shape[1])
-    full = fs.paged_quant_attention_cuda(wl.q, wl.cache)
+
+    def oq(t):
+        return O.OQuant(t.values.cpu().numpy(), t.scale.cpu().numpy(), t.zero_point.cpu().numpy(), 16,
+                        tuple(t.original_shape))
+
+    oc = O.OPagedCache(oq(wl.cache.k_quant), oq(wl.cache.v_quant), wl.cache.block_table.cpu().numpy(),
+                       wl.cache.lengths.cpu().numpy(), 16, int(wl.cache.max_seq_len))
+    full = torch.from_numpy(O.paged_quant_attention(wl.q.cpu().numpy(), oc).astype("float32")).to(wl.q.device)
     dec = SequenceShardedDecoder(transport="p2p")
     errs = []
     for _ in range(3):

@@ -142,6 +142,55 @@ def test_paged_from_dense_on_gpu_matches_reference_layout():
     np.testing.assert_array_equal(cache.block_table.cpu().numpy(), g["block_table"])
 
 
+def test_paged_accepts_foreign_cache_objects_built_by_the_reference():
+    """The golden pools were built by the reference's own PagedKVCache.from_dense
+    (src/flashspec/paged.py:303-419).  Wrapped in stand-in classes that carry only the
+    reference dataclasses' fields (QuantizedTensor quant.py:9-43, PagedKVCache
+    paged.py:258-300; the reference cannot be imported on a GPU box), the backend must
+    read them by duck typing and give the reference's output."""
+    from dataclasses import dataclass
+    from typing import Tuple
+
+    @dataclass(frozen=True)
+    class ForeignQuant:
+        values: torch.Tensor
+        scale: torch.Tensor
+        zero_point: torch.Tensor
+        block_size: int
+        original_shape: Tuple[int, ...]
+
+    @dataclass(frozen=True)
+    class ForeignPagedCache:
+        k_quant: ForeignQuant
+        v_quant: ForeignQuant
+        block_table: torch.Tensor
+        lengths: torch.Tensor
+        block_size: int
+        max_seq_len: int
+
+        @property
+        def num_heads(self) -> int:
+            return int(self.k_quant.original_shape[1])
+
+        def estimated_bytes(self) -> int:
+            qb = lambda t: t.values.numel() + 4 * t.scale.numel() + 2 * t.zero_point.numel()
+            return qb(self.k_quant) + qb(self.v_quant) + 8 * self.block_table.numel() + 8 * self.lengths.numel()
+
+    for name in ("paged_shuffled", "paged_gqa4"):
+        g = load_golden(name)
+
+        def fq(prefix):
+            return ForeignQuant(dev(g[f"{prefix}.values"]), dev(g[f"{prefix}.scale"]), dev(g[f"{prefix}.zero_point"]),
+                                int(g[f"{prefix}.block_size"]), tuple(int(x) for x in g[f"{prefix}.original_shape"]))
+
+        cache = ForeignPagedCache(fq("kq"), fq("vq"), dev(g["block_table"]), dev(g["lengths"]), 16,
+                                  int(g["max_seq_len"]))
+        out, stats = fs().paged_quant_attention_cuda(dev(g["q"]), cache, return_stats=True)
+        close(out, g["out"])
+        if "quant_kv_bytes" in g:
+            assert stats["quant_kv_bytes"] == float(g["quant_kv_bytes"])
+
+
 def _random_paged(rng, b, hq, hkv, lens, slack=3, layout="shuffled"):
     smax = max(max(lens), 1)
     q = rng.standard_normal((b, hq, 128)).astype(np.float16)

@@ -67,8 +67,37 @@ def _workload(seed=3, b=5, hq=8, hkv=4):
 
 
 def _close(got, ref):
-    err = (got.float() - ref.float()).abs()
-    assert bool(torch.all(err <= ATOL + RTOL * ref.float().abs())), f"max abs err {err.max().item():.3e}"
+    ref = torch.as_tensor(np.asarray(ref, dtype=np.float32)) if not torch.is_tensor(ref) else ref.float().cpu()
+    err = (got.float().cpu() - ref).abs()
+    assert bool(torch.all(err <= ATOL + RTOL * ref.abs())), f"max abs err {err.max().item():.3e}"
+
+
+def _oracle(q, cache):
+    """The CPU oracle's paged attention on the same quantized pool and table."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "oracle"))
+    import flashspec_oracle as O
+
+    def oq(t):
+        v, s, z = (x.cpu().numpy() for x in t)
+        return O.OQuant(v, s, z, 16, (v.shape[0], v.shape[1], 16, 128))
+
+    oc = O.OPagedCache(oq(cache["k"]), oq(cache["v"]), cache["table"].cpu().numpy(),
+                       cache["lengths"].cpu().numpy(), 16, cache["max_seq_len"])
+    return O.paged_quant_attention(q.cpu().numpy(), oc)
+
+
+def _noalloc_twice(lib, q, cache, splits):
+    stream = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for _ in range(2):  # the second call sees the first call's leftovers in the scratch
+        out = torch.full_like(q, float("nan"))
+        assert lib.fs_paged_decode_noalloc(C.byref(_args(q, cache, out, splits)), stream) == 0
+        outs.append(out)
+    torch.cuda.synchronize()
+    return outs
 
 
 @pytest.mark.gpu
@@ -81,6 +110,7 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     stream = torch.cuda.current_stream().cuda_stream
     q, cache = _workload()
     splits = 4  # forces the split-K path, i.e. the scratch memory
+    expected = _oracle(q, cache)
 
     ref = torch.empty_like(q)
     a = _args(q, cache, ref, splits)
@@ -92,22 +122,40 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     a.tickets, a.ticket_count = tickets.data_ptr(), tickets.numel()
     assert lib.fs_paged_decode(C.byref(a), stream) == 0
-
-    outs = []
-    for _ in range(2):  # the second call sees the first call's leftovers in the scratch
-        out = torch.full_like(q, float("nan"))
-        b = _args(q, cache, out, splits)
-        assert lib.fs_paged_decode_noalloc(C.byref(b), stream) == 0
-        outs.append(out)
     torch.cuda.synchronize()
-    for out in outs:
+    _close(ref, expected)
+
+    for out in _noalloc_twice(lib, q, cache, splits):
         assert not torch.isnan(out).any()
         _close(out, ref)
+        _close(out, expected)
     # the library's automatic split count goes through the same scratch
-    out = torch.empty_like(q)
-    assert lib.fs_paged_decode_noalloc(C.byref(_args(q, cache, out, 0)), stream) == 0
-    torch.cuda.synchronize()
-    _close(out, ref)
+    (out, _) = _noalloc_twice(lib, q, cache, 0)
+    _close(out, expected)
+
+
+@pytest.mark.gpu
+def test_noalloc_balanced_kernel_vs_oracle(monkeypatch):
+    """The balanced (stream-K) kernel merges the pieces of pairs that several warps
+    share through the same counters; through the fixed scratch it must clear them
+    itself before every call."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    from flashspec_b200 import _lib
+
+    lib = _lib.load()
+    q, cache = _workload(seed=11, b=5, hq=16, hkv=2)
+    expected = _oracle(q, cache)
+    monkeypatch.setenv("FLASHSPEC_DECODE_KERNEL", "balanced")
+    a = _args(q, cache, torch.empty_like(q), 0)
+    nbytes, s = C.c_size_t(0), C.c_int32(0)
+    assert lib.fs_decode_workspace_size(C.byref(a), C.byref(nbytes), C.byref(s)) == 0
+    assert s.value == 0 and nbytes.value > 0  # the balanced plan
+    # a split call first leaves its own partials behind in the shared scratch
+    _noalloc_twice(lib, q, cache, 7)
+    for out in _noalloc_twice(lib, q, cache, 0):
+        assert not torch.isnan(out).any()
+        _close(out, expected)
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
