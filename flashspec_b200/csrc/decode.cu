@@ -75,6 +75,7 @@ struct DecodeParams {
   float qk_scale_log2;
   int tier_ctas, skew;  // balanced kernel: CTAs per tier (the SM count) and the tier weight step
   int piece_cost;       // balanced kernel: virtual pages charged per (request, kv head) pair
+  int debug_mode;       // profiling only (FLASHSPEC_DEBUG_MODE)
 };
 
 // Shared-memory plan of one CTA: a ring of kNS page stages (K 2 KB + V 2 KB, 1024-byte
@@ -130,6 +131,10 @@ __device__ __forceinline__ void issue_page(const DecodeParams& p, const CUtensor
   tma_load_2d(dst, tmk, 0, (int32_t)(e * kPage), full, policy);
   tma_load_2d(dst + kPageBytes, tmv, 0, (int32_t)(e * kPage), full, policy);
   const uint32_t ms = meta_s + st * kMetaBytes;
+  if (p.debug_mode >= 3) {  // profiling: no qparam copies
+    mbar_arrive(full);
+    return;
+  }
   cp_async_4(ms + 0, p.k_scale + e);
   cp_async_4(ms + 4, p.v_scale + e);
   if (word_ok) {
@@ -1031,7 +1036,7 @@ __global__ void __maxnreg__(kMaxRegs)
     }
     if (j == 0) trace_mark<kTrace>(p, kW + 1, lane, 2);
     StageInfo si;
-    if (read_stage_info(meta_p, st, si)) {
+    if (read_stage_info(meta_p, st, si) && p.debug_mode != 2 && p.debug_mode != 4) {
       consume_page<0>(base_s + st * kStageBytes, off, empty_s + 8 * st, lane, si, qf, p.qk_scale_log2,
                       (lo + (int)(f - pair_P)) * kPage, len_eff, ws);
     } else {
@@ -1184,11 +1189,12 @@ static int smem_balanced(int shape, int batch) {
 }
 
 // FLASHSPEC_DEBUG_MODE (profiling only, results are wrong when set): 1 = skip the math,
-// 2 = data movement only.
+// 2 = data movement only (split kernel; the balanced kernel honours 2), 3 = no copies of
+// the pages' scale / zero-point words, 4 = 2 and 3 (balanced kernel).
 static int debug_mode() {
   const char* v = getenv("FLASHSPEC_DEBUG_MODE");
   const int m = v ? atoi(v) : 0;
-  return (m == 1 || m == 2) ? m : 0;
+  return (m >= 1 && m <= 4) ? m : 0;
 }
 
 static int shape_choice() {
@@ -1522,6 +1528,7 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.tier_ctas = device_sm_count(device);
   p.skew = tier_skew();
   p.piece_cost = piece_cost();
+  p.debug_mode = debug_mode();
   if (need > 0) {
     const size_t G = (size_t)p.G;
     const size_t units = pl.balanced ? (size_t)pl.ctas * kShapes[shape].warps * 2 * G
