@@ -17,7 +17,7 @@ FS_ERR_CUDA = 3
 FS_F16, FS_BF16, FS_F32 = 0, 1, 2
 FS_LAYOUT_CONTIGUOUS, FS_LAYOUT_PAGED = 0, 1
 FS_DEV_BAD_PAGE, FS_DEV_TIMEOUT = 1, 2
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _STATUS_EXC = {1: ValueError, 2: ValueError, 3: RuntimeError, 4: RuntimeError, 5: ValueError, 6: ValueError}
 
@@ -54,6 +54,8 @@ class FsDecodeArgs(C.Structure):
         ("tickets", C.c_void_p),
         ("ticket_count", C.c_int64),
         ("device_status", C.c_void_p),
+        ("q_dtype", C.c_int32),
+        ("page_size", C.c_int32),
     ]
 
 

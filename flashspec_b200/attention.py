@@ -76,8 +76,8 @@ def _validate_query(q: torch.Tensor, name: str) -> None:
         raise RuntimeError(f"CUDA {name} attention needs a CUDA q tensor")
     if q.shape[-1] > 256:
         raise ValueError(f"CUDA {name} attention supports head_dim <= 256")
-    if q.dtype != torch.float16:
-        raise ValueError("CUDA decode attention takes fp16 q")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("CUDA decode attention takes fp16 or bf16 q")
 
 
 def _check_gqa(hq: int, hkv: int) -> int:
@@ -111,7 +111,8 @@ def _run(entry: str, args: _lib.FsDecodeArgs, device: torch.device, splits_hint:
     return splits.value
 
 
-def _decode_args(layout, q, kq, vq, out, lengths, table, num_blocks, max_seq_len, hkv, status) -> _lib.FsDecodeArgs:
+def _decode_args(layout, q, kq, vq, out, lengths, table, num_blocks, max_seq_len, hkv, status,
+                 page_size: int = 0) -> _lib.FsDecodeArgs:
     a = _lib.FsDecodeArgs()
     a.layout = layout
     a.q = q.data_ptr()
@@ -127,6 +128,8 @@ def _decode_args(layout, q, kq, vq, out, lengths, table, num_blocks, max_seq_len
     a.max_seq_len = max_seq_len
     a.sm_scale = 1.0 / math.sqrt(float(q.shape[2]))
     a.device_status = status.data_ptr() if status is not None else None
+    a.q_dtype = _lib.FS_BF16 if q.dtype == torch.bfloat16 else _lib.FS_F16
+    a.page_size = int(page_size)
     return a
 
 
@@ -140,8 +143,9 @@ def fused_dequant_attention_cuda(q: torch.Tensor, k_quant, v_quant, lengths: Opt
                                  device_status: Optional[torch.Tensor] = None):
     """Contiguous INT8 KV decode attention (backend ``cuda_fused``).
 
-    q [B, Hq, D] fp16; k_quant/v_quant quantized from [B, Hkv, S, D] with
-    block_size 16; optional lengths int64 [B] (None = every request uses S).
+    q [B, Hq, D] fp16 or bf16 (out has q's dtype); k_quant/v_quant quantized from
+    [B, Hkv, S, D] (head_dim 32/64/128/256, quant block up to 64 tokens); optional
+    lengths int64 [B] (None = every request uses S).
     Validation follows _validate_triton_fused_inputs (triton_fused.py:506-548)."""
     _validate_query(q, "fused")
     if len(k_quant.original_shape) != 4 or len(v_quant.original_shape) != 4:
@@ -171,7 +175,7 @@ def fused_dequant_attention_cuda(q: torch.Tensor, k_quant, v_quant, lengths: Opt
     dense = 2 * b * hkv * seq * d * qc.element_size()
     quant = estimate_quantized_bytes(kq) + estimate_quantized_bytes(vq)
     return out, build_compression_stats(dense, quant, materializes_dense_kv=False, num_splits=splits,
-                                        block_n=PAGE_TOKENS, num_warps=NUM_WARPS)
+                                        block_n=int(kq.block_size), num_warps=NUM_WARPS)
 
 
 def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = False, *,
@@ -181,8 +185,9 @@ def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = Fals
     """Paged INT8 KV decode attention (backend ``cuda_paged``).
 
     ``cache`` is a PagedKVCache (this package's or the reference's): pool
-    [P, Hkv, 1, 16, D] int8 + fp32/int16 qparams, block_table int64 [B, cols]
-    (-1 = unallocated), lengths int64 [B], max_seq_len.  Validation follows
+    [P, Hkv, page / qb, qb, D] int8 + fp32/int16 qparams per quant block of qb tokens
+    (the page a multiple of qb), block_table int64 [B, cols] (-1 = unallocated),
+    lengths int64 [B], max_seq_len; q fp16 or bf16.  Validation follows
     _validate_triton_paged_inputs (triton_paged.py:302-335).
 
     Extensions used by sequence sharding: ``page_range=(lo, hi)`` restricts every
@@ -219,7 +224,7 @@ def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = Fals
     if partial_out is None:
         out = torch.empty_like(qc)
     a = _decode_args(_lib.FS_LAYOUT_PAGED, qc, kq, vq, out, lengths, table, num_pages, int(cache.max_seq_len),
-                     hkv, device_status)
+                     hkv, device_status, page_size=int(cache.block_size))
     if page_range is not None:
         a.page_begin, a.page_end = int(page_range[0]), int(page_range[1])
     if partial_out is not None:
@@ -235,7 +240,7 @@ def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = Fals
     dense = 2 * q.shape[0] * hkv * int(cache.max_seq_len) * d * qc.element_size()
     stats = build_compression_stats(dense, cache.estimated_bytes(), materializes_dense_kv=False,
                                     physical_blocks=float(cache.block_table.ge(0).sum().item()),
-                                    num_splits=splits, block_n=PAGE_TOKENS, num_warps=NUM_WARPS)
+                                    num_splits=splits, block_n=int(kq.block_size), num_warps=NUM_WARPS)
     return out, stats
 
 
@@ -252,7 +257,7 @@ def merge_partials(o_parts: torch.Tensor, lse_parts: torch.Tensor, out_dtype: to
     rows = lse_parts[0].numel()
     oc, lc = o_parts.contiguous(), lse_parts.contiguous()
     out = torch.empty(o_parts.shape[1:], dtype=out_dtype, device=o_parts.device)
-    code = {torch.float16: _lib.FS_F16, torch.float32: _lib.FS_F32}[out_dtype]
+    code = {torch.float16: _lib.FS_F16, torch.bfloat16: _lib.FS_BF16, torch.float32: _lib.FS_F32}[out_dtype]
     with torch.cuda.device(o_parts.device):
         _lib.check(_lib.load().fs_merge_partials(oc.data_ptr(), lc.data_ptr(), n, rows, d, 0, out.data_ptr(), code,
                                                  stream_of(o_parts.device)), "fs_merge_partials")

@@ -38,6 +38,7 @@
 
 #include "../../include/flashspec_b200.h"
 #include "common.h"
+#include "generic.h"
 #include "ptx.cuh"
 
 namespace fsb {
@@ -1449,6 +1450,12 @@ static size_t workspace_for(const FsDecodeArgs* a, int splits) {
   return align256(units * kD * 4) + align256(units * 4);
 }
 
+// The shapes of the tuned TMA kernels: D = 128, pages = quant blocks = 16 tokens, fp16 q.
+static bool tuned_shape(const FsDecodeArgs* a) {
+  return a->head_dim == kD && a->block_size == kPage && (a->page_size == 0 || a->page_size == kPage) &&
+         a->q_dtype == FS_F16;
+}
+
 static int validate(const FsDecodeArgs* a, int layout) {
   if (a == nullptr) return FS_ERR_INVALID_ARGUMENT;
   if (a->layout != layout) return FS_ERR_INVALID_ARGUMENT;
@@ -1456,7 +1463,10 @@ static int validate(const FsDecodeArgs* a, int layout) {
   if (a->q_heads % a->kv_heads) return FS_ERR_INVALID_ARGUMENT;
   const int G = a->q_heads / a->kv_heads;
   if (G > kMaxG) return FS_ERR_UNSUPPORTED;
-  if (a->head_dim != kD || a->block_size != kPage) return FS_ERR_UNSUPPORTED;
+  if (a->q_dtype != FS_F16 && a->q_dtype != FS_BF16) return FS_ERR_UNSUPPORTED;
+  if (a->block_size <= 0 || a->page_size < 0) return FS_ERR_INVALID_ARGUMENT;
+  if (layout == FS_LAYOUT_PAGED && a->page_size > 0 && a->page_size % a->block_size) return FS_ERR_INVALID_ARGUMENT;
+  if (!tuned_shape(a) && !generic_supports(a)) return FS_ERR_UNSUPPORTED;
   if (a->q == nullptr || a->k_values == nullptr || a->v_values == nullptr || a->k_scale == nullptr ||
       a->v_scale == nullptr || a->k_zero == nullptr || a->v_zero == nullptr)
     return FS_ERR_INVALID_ARGUMENT;
@@ -1465,10 +1475,11 @@ static int validate(const FsDecodeArgs* a, int layout) {
   if (a->num_blocks <= 0 || a->max_seq_len < 0) return FS_ERR_INVALID_ARGUMENT;
   if (layout == FS_LAYOUT_PAGED) {
     if (a->block_table == nullptr || a->lengths == nullptr || a->table_cols <= 0) return FS_ERR_INVALID_ARGUMENT;
-    if ((uint64_t)a->num_blocks * a->kv_heads * kPage >= (1ull << 31)) return FS_ERR_UNSUPPORTED;
+    const int64_t page = a->page_size > 0 ? a->page_size : a->block_size;
+    if ((uint64_t)a->num_blocks * a->kv_heads * page >= (1ull << 31)) return FS_ERR_UNSUPPORTED;
   } else {
-    if ((uint64_t)a->batch * a->kv_heads * a->num_blocks * kPage >= (1ull << 31)) return FS_ERR_UNSUPPORTED;
-    if ((int64_t)a->max_seq_len > a->num_blocks * kPage) return FS_ERR_INVALID_ARGUMENT;
+    if ((uint64_t)a->batch * a->kv_heads * a->num_blocks * a->block_size >= (1ull << 31)) return FS_ERR_UNSUPPORTED;
+    if ((int64_t)a->max_seq_len > a->num_blocks * a->block_size) return FS_ERR_INVALID_ARGUMENT;
   }
   if ((reinterpret_cast<uintptr_t>(a->k_values) | reinterpret_cast<uintptr_t>(a->v_values) |
        reinterpret_cast<uintptr_t>(a->q)) & 15)
@@ -1485,6 +1496,7 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   if (st != FS_OK) return st;
   int device = 0;
   if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+  if (!tuned_shape(a)) return launch_generic_decode(a, device, stream);
   const int forced = shape_choice();
   if ((st = configure_shapes<kPaged>(device, forced)) != FS_OK) return st;
   const Plan pl = make_plan(a, device, forced);
@@ -1561,6 +1573,12 @@ int fs_decode_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* spli
   if (st != FS_OK) return st;
   int device = 0;
   if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fsb::fail_cuda("cudaGetDevice", e);
+  if (!fsb::tuned_shape(a)) {
+    int splits = 1;
+    *bytes = fsb::generic_workspace(a, device, &splits);
+    if (splits_out) *splits_out = splits;
+    return FS_OK;
+  }
   const int forced = fsb::shape_choice();
   if ((st = fsb::configure_shapes<true>(device, forced)) != FS_OK) return st;
   const fsb::Plan pl = fsb::make_plan(a, device, forced);

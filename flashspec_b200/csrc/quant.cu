@@ -186,6 +186,8 @@ __global__ void merge_partials_kernel(const float* __restrict__ o, const float* 
   const float r = W > 0.f ? O / W : 0.f;
   if (out_dtype == FS_F16)
     reinterpret_cast<__half*>(out)[idx] = __float2half_rn(r);
+  else if (out_dtype == FS_BF16)
+    reinterpret_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(r);
   else
     reinterpret_cast<float*>(out)[idx] = r;
 }
@@ -257,7 +259,7 @@ int fs_merge_partials(const float* o_parts, const float* lse_parts, int32_t n_pa
                       int64_t part_stride, void* out, int32_t out_dtype, void* stream) {
   if (o_parts == nullptr || lse_parts == nullptr || out == nullptr || n_parts <= 0 || rows < 0 || head_dim <= 0)
     return FS_ERR_INVALID_ARGUMENT;
-  if (out_dtype != FS_F16 && out_dtype != FS_F32) return FS_ERR_UNSUPPORTED;
+  if (out_dtype != FS_F16 && out_dtype != FS_BF16 && out_dtype != FS_F32) return FS_ERR_UNSUPPORTED;
   const int64_t n = rows * head_dim;
   if (n == 0) return FS_OK;
   const int64_t blocks = (n + 255) / 256;

@@ -12,8 +12,10 @@
  *   contiguous KV : values [B, Hkv, nblk, 16, D], scale/zp [B, Hkv, nblk]
  *   paged KV pool : values [P, Hkv, 16, D],        scale/zp [P, Hkv]
  *   block_table   : int64 [B, cols], -1 = unallocated; lengths int64 [B]
- *   q / out       : fp16 [B, Hq, D]; q head h reads kv head h / (Hq/Hkv)
- * Current kernel limits: D = 128, block (page) size 16, Hq/Hkv in 1..8.
+ *   q / out       : fp16 or bf16 [B, Hq, D]; q head h reads kv head h / (Hq/Hkv)
+ * Shapes: head_dim 32/64/128/256, quant block 1..64 tokens (block * (D + 16) <= 12 KB),
+ * pages of one or more quant blocks, Hq/Hkv in 1..8.  D = 128 with pages and blocks of
+ * 16 tokens and fp16 q runs the tuned TMA kernels; every other shape the generic kernel.
  */
 #ifndef FLASHSPEC_B200_H_
 #define FLASHSPEC_B200_H_
@@ -25,7 +27,7 @@
 extern "C" {
 #endif
 
-#define FS_ABI_VERSION 1
+#define FS_ABI_VERSION 2
 
 typedef enum FsStatus {
   FS_OK = 0,
@@ -49,7 +51,7 @@ typedef enum FsKvLayout { FS_LAYOUT_CONTIGUOUS = 0, FS_LAYOUT_PAGED = 1 } FsKvLa
 /* Arguments of one decode-attention call (one query token per request). */
 typedef struct FsDecodeArgs {
   int32_t layout;             /* FsKvLayout                                          */
-  const void* q;              /* fp16 [B, Hq, D]                                     */
+  const void* q;              /* [B, Hq, D], dtype q_dtype                            */
   const int8_t* k_values;     /* see layouts above; 16-byte aligned                  */
   const float* k_scale;
   const int16_t* k_zero;      /* 4-byte aligned                                      */
@@ -58,7 +60,7 @@ typedef struct FsDecodeArgs {
   const int16_t* v_zero;
   const int64_t* block_table; /* paged: [B, table_cols]; contiguous: NULL            */
   const int64_t* lengths;     /* [B]; NULL (contiguous only) = every request is seq_len */
-  void* out;                  /* fp16 [B, Hq, D]; unused when shard_o is set          */
+  void* out;                  /* q_dtype [B, Hq, D]; unused when shard_o is set       */
   int32_t batch, q_heads, kv_heads, head_dim, block_size;
   int64_t num_blocks;         /* paged: physical pages P; contiguous: nblk per (b,h)  */
   int32_t table_cols;         /* paged only                                          */
@@ -81,6 +83,9 @@ typedef struct FsDecodeArgs {
                                  that completes leaves them zero                    */
   int64_t ticket_count;
   uint32_t* device_status;    /* optional device word receiving FS_DEV_* bits         */
+  int32_t q_dtype;            /* FsDtype of q and out: FS_F16 or FS_BF16              */
+  int32_t page_size;          /* paged: tokens per page, a multiple of block_size
+                                 (0 = block_size); contiguous: ignored                 */
 } FsDecodeArgs;
 
 /* Library version / ABI check. */
