@@ -564,7 +564,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if not args.no_extras and cfg == "cfg1":
         extras["seqshard"] = seqshard_sub(args, rank, world, dev, timer)
         if world == 1:
-            extras["paged_vs_contiguous"] = paged_vs_contiguous(args, wl, timer, elapsed_ms / args.steps)
+            extras["paged_vs_contiguous"] = paged_vs_contiguous(args, wl, timer)
+            extras["other_configs"] = other_configs(args, timer, dev)
     read_gbs = read_probe_gbs(dev) if (rank == 0 and not args.no_extras) else None
     if rank != 0:
         return
@@ -634,7 +635,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     print(json.dumps(line), flush=True)
 
 
-def paged_vs_contiguous(args, wl, timer, paged_ms: float):
+def paged_vs_contiguous(args, wl, timer):
     """The cfg1 KV in the contiguous layout through the fused entry point, same run.  The
     two are timed alternately (five rounds each, median), both with the same lengths,
     so clock drift under the power cap does not favour either."""
@@ -668,6 +669,57 @@ def paged_vs_contiguous(args, wl, timer, paged_ms: float):
             "outputs_bit_identical": same, "rounds": 5, "calls_per_round": n,
             "note": "same int8 bytes and lengths; contiguous = values [B, H, nblk, 16, D] through fs_fused_decode; "
                     "alternating rounds, medians"}
+
+
+def other_configs(args, timer, dev):
+    """cfg0 (contiguous, four rotated input copies), cfg2 (ragged GQA at its configured
+    4 splits and on the default plan) and cfg4 (the serving loop), each on this GPU, so
+    one default run records every configuration's device time."""
+    import torch
+
+    import flashspec_b200 as fs
+    from flashspec_b200 import configs
+    from flashspec_b200.serving import ServingConfig, run
+
+    peak, _ = measured_peaks()
+    n = max(50, min(args.steps, 500))
+    res = {}
+
+    def line(name, nbytes, ms, **kw):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"us_per_call": ms * 1e3, "tb_s": gbs / 1e3, "frac_of_copy_peak": gbs / peak,
+                     "frac_of_nominal_8tbs": gbs / NOMINAL_HBM_GBS, "bytes_per_call": nbytes, "calls": n, **kw}
+
+    wl0 = configs.cfg0()
+    copies = [(wl0.q, wl0.k_quant, wl0.v_quant)]
+    for _ in range(3):
+        copies.append((wl0.q.clone(), *(fs.QuantizedTensor(t.values.clone(), t.scale.clone(), t.zero_point.clone(), 16,
+                                                           t.original_shape) for t in (wl0.k_quant, wl0.v_quant))))
+    step0 = lambda i: fs.fused_dequant_attention_cuda(*copies[i % 4])
+    for i in range(8):
+        step0(i)
+    line("cfg0", wl0.bytes_per_call, timer.run(step0, n) / n, l2="four rotated input copies")
+    del copies, wl0, step0
+    torch.cuda.empty_cache()
+
+    wl2 = configs.cfg2()
+    for splits, tag in [(4, "cfg2_splits4"), (None, "cfg2_default_plan")]:
+        step2 = lambda i: fs.paged_quant_attention_cuda(wl2.q, wl2.cache, num_splits=splits)
+        for i in range(8):
+            step2(i)
+        line(tag, wl2.bytes_per_call, timer.run(step2, n) / n)
+    del wl2
+    torch.cuda.empty_cache()
+
+    sc = ServingConfig(steps=2000, seed=0)
+    r = run(sc, device=dev)
+    res["cfg4"] = {"step_ms_mean": r["step_ms_mean"], "tokens_per_s_device": r["tokens_per_s_device"],
+                   "attention_tb_s": r["attention_tbps"], "append_tb_s": r["append_tbps"],
+                   "attention_frac_of_copy_peak": r["attention_tbps"] * 1e3 / peak,
+                   "append_ms_per_step": r["append_ms_total"] / r["steps_measured"],
+                   "gpu_launches": r["gpu_launches"], "steps": sc.steps}
+    torch.cuda.empty_cache()
+    return res
 
 
 def seqshard_sub(args, rank: int, world: int, dev, timer):

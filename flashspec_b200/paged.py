@@ -164,16 +164,42 @@ class PagedKVCache:
                    block_size, s)
 
     def to_dense(self) -> Tuple[torch.Tensor, torch.Tensor]:
-        """paged.py:421-461 (inspection utility; attention never calls it)."""
-        pk = dequantize_int8_per_block(self.k_quant, dtype=torch.float32)
-        pv = dequantize_int8_per_block(self.v_quant, dtype=torch.float32)
+        """paged.py:421-461 (inspection utility; attention never calls it): dense fp32
+        K/V [B, H, max_seq_len, D], unallocated table entries read page 0 as in the
+        reference (``table.clamp_min(0)``).  With one quantization block per page, only
+        the pages the table references are dequantized (``fs_dequantize_pages``, gathered
+        by the kernel); otherwise the whole pool is dequantized with torch ops."""
         table = self.block_table.clamp_min(0)
+        kq, vq = self.k_quant, self.v_quant
+        page = int(self.block_size)
+        if int(kq.block_size) == page and kq.values.is_cuda:
+            from . import _lib
+            from .quant import stream_of
 
-        def gather(p):
+            pages = table.reshape(-1).to(torch.int64).contiguous()
+            b, cols = table.shape
+
+            def gather(qt):
+                out = torch.empty((pages.numel(), self.num_heads, page, self.head_dim), dtype=torch.float32,
+                                  device=qt.values.device)
+                with torch.cuda.device(qt.values.device):
+                    _lib.check(_lib.load().fs_dequantize_pages(
+                        qt.values.contiguous().data_ptr(), qt.scale.contiguous().data_ptr(),
+                        qt.zero_point.contiguous().data_ptr(), pages.data_ptr(), pages.numel(),
+                        int(qt.values.shape[0]), self.num_heads, page, self.head_dim, out.data_ptr(),
+                        stream_of(qt.values.device)), "fs_dequantize_pages")
+                return (out.view(b, cols, self.num_heads, page, self.head_dim).permute(0, 2, 1, 3, 4)
+                        .reshape(b, self.num_heads, -1, self.head_dim)[..., : self.max_seq_len, :])
+
+            return gather(kq), gather(vq)
+        pk = dequantize_int8_per_block(kq, dtype=torch.float32)
+        pv = dequantize_int8_per_block(vq, dtype=torch.float32)
+
+        def gather_t(p):
             return (p[table].permute(0, 2, 1, 3, 4).contiguous()
                     .reshape(self.batch_size, self.num_heads, -1, self.head_dim)[..., : self.max_seq_len, :])
 
-        return gather(pk), gather(pv)
+        return gather_t(pk), gather_t(pv)
 
     def append(self, k_new: torch.Tensor, v_new: torch.Tensor) -> "PagedKVCache":
         """Functional append (paged.py:463-557) on the GPU, bit-exact: every page of the

@@ -191,6 +191,27 @@ def test_paged_accepts_foreign_cache_objects_built_by_the_reference():
             assert stats["quant_kv_bytes"] == float(g["quant_kv_bytes"])
 
 
+@pytest.mark.parametrize("layout", ["shuffled", "interleaved"])
+def test_to_dense_matches_reference_bit_exact(layout):
+    """PagedKVCache.to_dense (fs_dequantize_pages gathering the referenced pages) against
+    the reference's to_dense recorded in the golden (paged.py:421-461): bit-identical."""
+    g = load_golden(f"paged_{layout}")
+    cache = paged_from_golden(g)
+    k, v = cache.to_dense()
+    ok, ov = O.paged_to_dense(O.OPagedCache(g.quant("kq"), g.quant("vq"), g["block_table"], g["lengths"], 16,
+                                            int(g["max_seq_len"])))
+    np.testing.assert_array_equal(k.cpu().numpy().view(np.uint32), ok.astype(np.float32).view(np.uint32))
+    np.testing.assert_array_equal(v.cpu().numpy().view(np.uint32), ov.astype(np.float32).view(np.uint32))
+    # unallocated entries read page 0, as the reference's clamp_min(0) gather does
+    t = cache.block_table.clone()
+    t[0, -1] = -1
+    c2 = fs().PagedKVCache(cache.k_quant, cache.v_quant, t, cache.lengths, 16, cache.max_seq_len)
+    k2, _ = c2.to_dense()
+    ok2, _ = O.paged_to_dense(O.OPagedCache(g.quant("kq"), g.quant("vq"), t.cpu().numpy(), g["lengths"], 16,
+                                            int(g["max_seq_len"])))
+    np.testing.assert_array_equal(k2.cpu().numpy(), ok2.astype(np.float32))
+
+
 def _random_paged(rng, b, hq, hkv, lens, slack=3, layout="shuffled"):
     smax = max(max(lens), 1)
     q = rng.standard_normal((b, hq, 128)).astype(np.float16)
