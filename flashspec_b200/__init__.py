@@ -17,6 +17,7 @@ from .attention import (BACKENDS, fused_dequant_attention_cuda, get_backend, mer
 from .paged import PagedKVAllocator, PagedKVCache
 from .quant import (QuantizedTensor, build_compression_stats, dequantize_int8_per_block,
                     estimate_quantized_bytes, quantize_int8_per_block)
+from .tree import tree_verify_attention_cuda
 
 __all__ = [
     "BACKENDS",
@@ -34,4 +35,5 @@ __all__ = [
     "quantize_int8_per_block",
     "register_backend",
     "reset_workspaces",
+    "tree_verify_attention_cuda",
 ]

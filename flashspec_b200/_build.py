@@ -16,7 +16,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = ROOT / "_build"
 LIB = PKG / "libflashspec_b200.so"
-SOURCES = ["decode.cu", "decode_generic.cu", "quant.cu", "noalloc.cu", "exchange.cu", "probe.cu"]
+SOURCES = ["decode.cu", "decode_generic.cu", "quant.cu", "noalloc.cu", "exchange.cu", "probe.cu", "tree.cu"]
 HEADERS = ["ptx.cuh", "common.h", "generic.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", f"-I{ROOT / 'include'}"]

@@ -135,6 +135,25 @@ class FsExchangeArgs(C.Structure):
     ]
 
 
+class FsTreeArgs(C.Structure):
+    _fields_ = [
+        ("q", C.c_void_p),
+        ("tree_k", C.c_void_p),
+        ("tree_v", C.c_void_p),
+        ("parents", C.c_void_p),
+        ("prefix_o", C.c_void_p),
+        ("prefix_lse", C.c_void_p),
+        ("out", C.c_void_p),
+        ("batch", C.c_int32),
+        ("nodes", C.c_int32),
+        ("q_heads", C.c_int32),
+        ("kv_heads", C.c_int32),
+        ("head_dim", C.c_int32),
+        ("q_dtype", C.c_int32),
+        ("sm_scale", C.c_float),
+    ]
+
+
 # every symbol the header declares, with its signature
 SIGNATURES = {
     "fs_abi_version": (C.c_int, []),
@@ -153,6 +172,7 @@ SIGNATURES = {
     "fs_exchange_destroy": (C.c_int, [C.c_void_p]),
     "fs_exchange_merge": (C.c_int, [C.POINTER(FsExchangeArgs), C.c_void_p]),
     "fs_page_update": (C.c_int, [C.POINTER(FsPageUpdateArgs), C.c_void_p]),
+    "fs_tree_attend": (C.c_int, [C.POINTER(FsTreeArgs), C.c_void_p]),
     "fs_read_bandwidth_probe": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int32, C.POINTER(C.c_int32),
                                           C.c_void_p]),
     "fs_dequantize_pages": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,

@@ -237,6 +237,28 @@ int fs_dequantize_pages(const int8_t* values, const float* scale, const int16_t*
                         const int64_t* pages, int64_t n_pages_listed, int64_t num_pages, int32_t heads,
                         int32_t block_size, int32_t head_dim, float* out, void* stream);
 
+/* Tree-attention verify (speculative decoding), the draft-tree half: for node i of
+ * request b, attention of q [B, nodes, Hq, D] over the draft tokens on i's root path
+ * (tree_k / tree_v [B, nodes, Hkv, D], parents int32 [B, nodes], parents[b][i] < i,
+ * -1 = the node hangs off the committed prefix), merged with the normalised partial
+ * (prefix_o fp32 [B, nodes, Hq, D], prefix_lse fp32 [B, nodes, Hq], natural log) of the
+ * same rows over the committed prefix, or with nothing when prefix_o is NULL.  out has
+ * q's dtype (FS_F16 / FS_BF16); head_dim 32/64/128/256.  The reference plans this kernel
+ * (doc/TODO.MD:186-237, "Kernel 3") without implementing it; parents are validated by
+ * the caller (the Python wrapper raises on cycles and orphans). */
+typedef struct FsTreeArgs {
+  const void* q;
+  const void* tree_k;
+  const void* tree_v;
+  const int32_t* parents;
+  const float* prefix_o;
+  const float* prefix_lse;
+  void* out;
+  int32_t batch, nodes, q_heads, kv_heads, head_dim, q_dtype;
+  float sm_scale;
+} FsTreeArgs;
+int fs_tree_attend(const FsTreeArgs* args, void* stream);
+
 /* Measurement aid, no counterpart in the reference: streams `bytes` (a multiple of 16,
  * 16-byte aligned buffer) through a read-only kernel and stores one 32-bit XOR per CTA
  * into sink[0 .. *ctas_used) (sink_count entries at least as many as the CTAs used, at

@@ -446,6 +446,54 @@ def merge_partials(o: np.ndarray, lse: np.ndarray) -> np.ndarray:
     return np.where(den[..., None] > 0, num / np.where(den > 0, den, 1.0)[..., None], 0.0).astype(F32)
 
 
+# ---------------------------------------------------------------------------
+# tree-attention verify -- doc/TODO.MD:186-237 (planned in the reference, not implemented)
+# ---------------------------------------------------------------------------
+
+
+def tree_mask(parents: np.ndarray) -> np.ndarray:
+    """Dense tree mask [B, N, N]: mask[b, i, j] is True when draft node j is node i or
+    one of its ancestors (parents[b, i] < i, -1 = root hangs off the committed prefix)."""
+    b, n = parents.shape
+    m = np.zeros((b, n, n), bool)
+    for bi in range(b):
+        for i in range(n):
+            j = i
+            while j >= 0:
+                m[bi, i, j] = True
+                j = int(parents[bi, j])
+    return m
+
+
+def tree_verify_attention(q: np.ndarray, cache: OPagedCache, tree_k: np.ndarray, tree_v: np.ndarray,
+                          parents: np.ndarray) -> np.ndarray:
+    """The dense-mask statement of tree verify: node i of request b attends to the
+    committed prefix (the first lengths[b] tokens of the paged cache, dequantized as the
+    reference's to_dense does) and to the draft tokens the tree mask allows, fp32 softmax
+    with scale 1/sqrt(D), output cast to q's dtype.  q [B, N, Hq, D], tree_k/v
+    [B, N, Hkv, D]; GQA as elsewhere (q head h reads kv head h // (Hq / Hkv))."""
+    b, n, hq, d = q.shape
+    kd, vd = paged_to_dense(cache)  # [B, Hkv, S, D]
+    hkv = kd.shape[1]
+    g = hq // hkv
+    s = kd.shape[2]
+    mask = tree_mask(parents)
+    out = np.zeros(q.shape, np.float32)
+    scale = F32(1.0 / math.sqrt(d))
+    for bi in range(b):
+        L = min(int(cache.lengths[bi]), s)
+        for h in range(hq):
+            kh = h // g
+            keys = np.concatenate([kd[bi, kh, :L], tree_k[bi, :, kh].astype(F32)], 0)  # [L + N, D]
+            vals = np.concatenate([vd[bi, kh, :L], tree_v[bi, :, kh].astype(F32)], 0)
+            sc = (keys @ q[bi, :, h].astype(F32).T).T * scale  # [N, L + N]
+            allowed = np.concatenate([np.ones((n, L), bool), mask[bi]], 1)
+            sc = np.where(allowed, sc, -np.inf)
+            w = np.exp(sc - sc.max(1, keepdims=True))
+            out[bi, :, h] = (w / w.sum(1, keepdims=True)) @ vals
+    return out.astype(q.dtype)
+
+
 def algorithmic_bytes_paged(batch: int, q_heads: int, kv_heads: int, head_dim: int, lengths: Sequence[int],
                             page: int = 16, table_cols: Optional[int] = None, q_bytes: int = 2) -> int:
     """Algorithmic bytes of one paged decode call: for every referenced (page, kv

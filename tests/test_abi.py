@@ -48,7 +48,7 @@ def test_ctypes_layouts_match_c(tmp_path):
 
     structs = {"FsDecodeArgs": _lib.FsDecodeArgs, "FsQuantizeArgs": _lib.FsQuantizeArgs,
                "FsPageUpdate": _lib.FsPageUpdate, "FsPageUpdateArgs": _lib.FsPageUpdateArgs,
-               "FsExchangeArgs": _lib.FsExchangeArgs}
+               "FsExchangeArgs": _lib.FsExchangeArgs, "FsTreeArgs": _lib.FsTreeArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', "int main(void){"]
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')

@@ -132,3 +132,34 @@ def test_merge_partials_equals_full_attention():
 
 def test_algorithmic_bytes_matches_baseline_cfg1():
     assert O.algorithmic_bytes_paged(16, 32, 32, 128, [4096] * 16) == 538_738_816
+
+
+def test_tree_verify_oracle_equals_path_gather():
+    """The dense-mask statement of tree verify agrees with gathering each node's root path
+    explicitly (two independent restatements), including a chain, a fork and a node that
+    hangs off the prefix."""
+    rng = np.random.default_rng(5)
+    b, n, hq, hkv, d = 2, 6, 4, 2, 16
+    q = rng.standard_normal((b, n, hq, d)).astype(np.float32)
+    k = rng.standard_normal((b, hkv, 40, d)).astype(np.float32)
+    v = rng.standard_normal((b, hkv, 40, d)).astype(np.float32)
+    cache = O.paged_from_dense(k, v, 8, lengths=np.array([40, 13]))
+    tk = rng.standard_normal((b, n, hkv, d)).astype(np.float32)
+    tv = rng.standard_normal((b, n, hkv, d)).astype(np.float32)
+    parents = np.array([[-1, 0, 1, 1, 0, -1], [-1, 0, 1, 2, 3, 4]])
+    got = O.tree_verify_attention(q, cache, tk, tv, parents)
+    kd, vd = O.paged_to_dense(cache)
+    for bi in range(b):
+        L = int(cache.lengths[bi])
+        for i in range(n):
+            path, j = [], i
+            while j >= 0:
+                path.append(j)
+                j = int(parents[bi, j])
+            for h in range(hq):
+                kh = h // (hq // hkv)
+                keys = np.concatenate([kd[bi, kh, :L], tk[bi, path, kh]], 0)
+                vals = np.concatenate([vd[bi, kh, :L], tv[bi, path, kh]], 0)
+                sc = keys @ q[bi, i, h] / np.sqrt(d)
+                w = np.exp(sc - sc.max())
+                np.testing.assert_allclose(got[bi, i, h], (w / w.sum()) @ vals, rtol=1e-5, atol=1e-6)
