@@ -15,8 +15,10 @@ from ._build import build
 from .attention import (BACKENDS, fused_dequant_attention_cuda, get_backend, merge_partials,
                         paged_quant_attention_cuda, register_backend, reset_workspaces)
 from .paged import PagedKVAllocator, PagedKVCache
-from .quant import (QuantizedTensor, build_compression_stats, dequantize_int8_per_block,
-                    estimate_quantized_bytes, quantize_int8_per_block)
+from .paged import paged_cache_symmetric
+from .quant import (QuantizedTensor, SymQuantizedTensor, build_compression_stats, dequantize_int8_per_block,
+                    dequantize_int8_symmetric, estimate_quantized_bytes, quantize_int8_per_block,
+                    quantize_int8_symmetric_per_token)
 from .tree import tree_verify_attention_cuda
 
 __all__ = [
@@ -34,6 +36,10 @@ __all__ = [
     "paged_quant_attention_cuda",
     "quantize_int8_per_block",
     "register_backend",
+    "SymQuantizedTensor",
+    "dequantize_int8_symmetric",
+    "paged_cache_symmetric",
+    "quantize_int8_symmetric_per_token",
     "reset_workspaces",
     "tree_verify_attention_cuda",
 ]

@@ -17,7 +17,8 @@ FS_ERR_CUDA = 3
 FS_F16, FS_BF16, FS_F32 = 0, 1, 2
 FS_LAYOUT_CONTIGUOUS, FS_LAYOUT_PAGED = 0, 1
 FS_DEV_BAD_PAGE, FS_DEV_TIMEOUT = 1, 2
-ABI_VERSION = 2
+ABI_VERSION = 3
+FS_KV_AFFINE_BLOCK, FS_KV_SYMMETRIC = 0, 1
 
 _STATUS_EXC = {1: ValueError, 2: ValueError, 3: RuntimeError, 4: RuntimeError, 5: ValueError, 6: ValueError}
 
@@ -56,6 +57,7 @@ class FsDecodeArgs(C.Structure):
         ("device_status", C.c_void_p),
         ("q_dtype", C.c_int32),
         ("page_size", C.c_int32),
+        ("kv_format", C.c_int32),
     ]
 
 
@@ -166,6 +168,7 @@ SIGNATURES = {
     "fs_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int64, C.c_void_p,
                                     C.c_int32, C.c_void_p]),
     "fs_quantize_blocks": (C.c_int, [C.POINTER(FsQuantizeArgs), C.c_void_p]),
+    "fs_quantize_symmetric": (C.c_int, [C.POINTER(FsQuantizeArgs), C.c_void_p]),
     "fs_exchange_create": (C.c_int, [C.c_int64, C.POINTER(C.c_void_p), C.c_void_p]),
     "fs_exchange_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "fs_exchange_close": (C.c_int, [C.c_void_p]),

@@ -19,7 +19,8 @@ from typing import Dict, Optional, Tuple
 import torch
 
 from . import _lib
-from .quant import QuantizedTensor, build_compression_stats, estimate_quantized_bytes, require_cuda, stream_of
+from .quant import (QuantizedTensor, SymQuantizedTensor, build_compression_stats, estimate_quantized_bytes,
+                    require_cuda, stream_of)
 
 PAGE_TOKENS = 16  # tokens per kernel step (one page / quant block)
 NUM_WARPS = 4
@@ -116,8 +117,14 @@ def _decode_args(layout, q, kq, vq, out, lengths, table, num_blocks, max_seq_len
     a = _lib.FsDecodeArgs()
     a.layout = layout
     a.q = q.data_ptr()
-    a.k_values, a.k_scale, a.k_zero = kq.values.data_ptr(), kq.scale.data_ptr(), kq.zero_point.data_ptr()
-    a.v_values, a.v_scale, a.v_zero = vq.values.data_ptr(), vq.scale.data_ptr(), vq.zero_point.data_ptr()
+    sym = bool(getattr(kq, "symmetric", False))
+    if sym != bool(getattr(vq, "symmetric", False)):
+        raise ValueError("K and V must use the same quantization format")
+    a.kv_format = _lib.FS_KV_SYMMETRIC if sym else _lib.FS_KV_AFFINE_BLOCK
+    a.k_values, a.k_scale = kq.values.data_ptr(), kq.scale.data_ptr()
+    a.v_values, a.v_scale = vq.values.data_ptr(), vq.scale.data_ptr()
+    if not sym:
+        a.k_zero, a.v_zero = kq.zero_point.data_ptr(), vq.zero_point.data_ptr()
     a.block_table = table.data_ptr() if table is not None else None
     a.lengths = lengths.data_ptr() if lengths is not None else None
     a.out = out.data_ptr() if out is not None else None
@@ -133,7 +140,10 @@ def _decode_args(layout, q, kq, vq, out, lengths, table, num_blocks, max_seq_len
     return a
 
 
-def _contig_quant(qt) -> QuantizedTensor:
+def _contig_quant(qt):
+    if getattr(qt, "symmetric", False):
+        return SymQuantizedTensor(qt.values.contiguous(), qt.scale.contiguous(), int(qt.block_size),
+                                  tuple(qt.original_shape))
     return QuantizedTensor(qt.values.contiguous(), qt.scale.contiguous(), qt.zero_point.contiguous(),
                            int(qt.block_size), tuple(qt.original_shape))
 
@@ -165,7 +175,9 @@ def fused_dequant_attention_cuda(q: torch.Tensor, k_quant, v_quant, lengths: Opt
             raise RuntimeError("lengths must be on q's CUDA device")
         lengths = _i64(lengths)
     kq, vq = _contig_quant(k_quant), _contig_quant(v_quant)
-    nblk = int(kq.values.shape[-3])
+    # quant blocks per (request, kv head); the symmetric format stores [.., S_pad, D]
+    nblk = (int(kq.values.shape[-2]) // int(kq.block_size) if getattr(kq, "symmetric", False)
+            else int(kq.values.shape[-3]))
     qc = q.contiguous()
     out = torch.empty_like(qc)
     a = _decode_args(_lib.FS_LAYOUT_CONTIGUOUS, qc, kq, vq, out, lengths, None, nblk, seq, hkv, device_status)

@@ -1452,7 +1452,7 @@ static size_t workspace_for(const FsDecodeArgs* a, int splits) {
 
 // The shapes of the tuned TMA kernels: D = 128, pages = quant blocks = 16 tokens, fp16 q.
 static bool tuned_shape(const FsDecodeArgs* a) {
-  return a->head_dim == kD && a->block_size == kPage && (a->page_size == 0 || a->page_size == kPage) &&
+  return a->kv_format == FS_KV_AFFINE_BLOCK && a->head_dim == kD && a->block_size == kPage && (a->page_size == 0 || a->page_size == kPage) &&
          a->q_dtype == FS_F16;
 }
 
@@ -1467,8 +1467,11 @@ static int validate(const FsDecodeArgs* a, int layout) {
   if (a->block_size <= 0 || a->page_size < 0) return FS_ERR_INVALID_ARGUMENT;
   if (layout == FS_LAYOUT_PAGED && a->page_size > 0 && a->page_size % a->block_size) return FS_ERR_INVALID_ARGUMENT;
   if (!tuned_shape(a) && !generic_supports(a)) return FS_ERR_UNSUPPORTED;
+  if (a->kv_format != FS_KV_AFFINE_BLOCK && a->kv_format != FS_KV_SYMMETRIC) return FS_ERR_INVALID_ARGUMENT;
   if (a->q == nullptr || a->k_values == nullptr || a->v_values == nullptr || a->k_scale == nullptr ||
-      a->v_scale == nullptr || a->k_zero == nullptr || a->v_zero == nullptr)
+      a->v_scale == nullptr)
+    return FS_ERR_INVALID_ARGUMENT;
+  if (a->kv_format == FS_KV_AFFINE_BLOCK && (a->k_zero == nullptr || a->v_zero == nullptr))
     return FS_ERR_INVALID_ARGUMENT;
   if (a->shard_o == nullptr && a->out == nullptr) return FS_ERR_INVALID_ARGUMENT;
   if ((a->shard_o == nullptr) != (a->shard_lse == nullptr)) return FS_ERR_INVALID_ARGUMENT;

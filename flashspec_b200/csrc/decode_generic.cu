@@ -52,6 +52,7 @@ struct GenericParams {
   float* part_lse;  // [S][B * Hq]
   uint32_t* status;
   int B, Hq, Hkv, G, S, cols, qb, bpp, paged, bf16;
+  int sym;             // FS_KV_SYMMETRIC: per-token scales, no zero points
   int64_t num_blocks;  // paged: pages; contiguous: quant blocks per (request, kv head)
   int64_t max_seq_len, page_begin, page_end;
   float qk_scale_log2;
@@ -155,8 +156,10 @@ __global__ void __launch_bounds__(kGW * 32) decode_generic_kernel(const GenericP
     cp_async_wait_prev();
     __syncwarp();
     if (e_cur >= 0) {
-      const float ksc = p.kscale[e_cur], vsc = p.vscale[e_cur];
-      const float kz = (float)p.kzero[e_cur], vz = (float)p.vzero[e_cur];
+      // affine: one (scale, zero point) per unit, values stored as u - 128; symmetric:
+      // one scale per token (read per lane / per token below), values as stored
+      const float ksc_u = p.sym ? 1.f : p.kscale[e_cur], vsc_u = p.sym ? 1.f : p.vscale[e_cur];
+      const float kz = p.sym ? 128.f : (float)p.kzero[e_cur], vz = p.sym ? 128.f : (float)p.vzero[e_cur];
       const uint8_t* kd = wbuf + (size_t)b * 2 * unit_bytes;
       const uint8_t* vd = kd + unit_bytes;
       for (int t0 = 0; t0 < qb; t0 += 32) {
@@ -195,6 +198,9 @@ __global__ void __launch_bounds__(kGW * 32) decode_generic_kernel(const GenericP
           }
         }
         const bool valid = lane < nt && tok < len;
+        const size_t tok_at = (size_t)e_cur * qb + t0 + lane;  // this lane's token in the scale arrays
+        const float ksc = p.sym ? (lane < nt ? p.kscale[tok_at] : 0.f) : ksc_u;
+        const float vsc = p.sym ? (lane < nt ? p.vscale[tok_at] : 0.f) : vsc_u;
         // ---- online softmax per query (log2 domain)
 #pragma unroll
         for (int g = 0; g < kGMaxG; ++g) {
@@ -309,6 +315,7 @@ bool generic_supports(const FsDecodeArgs* a) {
   const int page = a->page_size > 0 ? a->page_size : qb;
   if (a->layout == FS_LAYOUT_PAGED && page % qb) return false;
   if (a->q_heads / a->kv_heads > kGMaxG) return false;
+  if (a->kv_format == FS_KV_SYMMETRIC && a->layout == FS_LAYOUT_PAGED && page != qb) return false;
   return a->q_dtype == FS_F16 || a->q_dtype == FS_BF16;
 }
 
@@ -373,6 +380,7 @@ int launch_generic_decode(const FsDecodeArgs* a, int device, void* stream) {
   p.bpp = a->layout == FS_LAYOUT_PAGED ? (a->page_size > 0 ? a->page_size : a->block_size) / a->block_size : 1;
   p.paged = a->layout == FS_LAYOUT_PAGED;
   p.bf16 = a->q_dtype == FS_BF16;
+  p.sym = a->kv_format == FS_KV_SYMMETRIC;
   p.num_blocks = a->num_blocks;
   p.max_seq_len = a->max_seq_len;
   p.page_begin = a->page_begin;

@@ -192,9 +192,43 @@ __global__ void merge_partials_kernel(const float* __restrict__ o, const float* 
     reinterpret_cast<float*>(out)[idx] = r;
 }
 
+// Symmetric per-token quantization (the format of the benchmark configurations'
+// wording, doc/TODO.MD:241-255 "symmetric INT8"): one fp32 scale per (token, head),
+// scale = max(absmax / 127, 1e-8), q = clamp(rint(x / scale), -127, 127), each step an
+// explicitly rounded fp32 operation.  One warp per token row of D values.
+__global__ void quantize_sym_kernel(const void* __restrict__ x, int dtype, int64_t rows, int D,
+                                    int8_t* __restrict__ values, float* __restrict__ scale) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float amax = 0.f;
+  for (int d = lane; d < D; d += 32) amax = fmaxf(amax, fabsf(load_as_f32(x, row * D + d, dtype)));
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1.0e-8f);
+  for (int d = lane; d < D; d += 32) {
+    const float q = fminf(fmaxf(rintf(__fdiv_rn(load_as_f32(x, row * D + d, dtype), s)), -127.0f), 127.0f);
+    values[row * D + d] = (int8_t)(int)q;
+  }
+  if (lane == 0) scale[row] = s;
+}
+
 }  // namespace fsb
 
 extern "C" {
+
+/* args->x is [n_lead, seq_len, head_dim]; writes values [n_lead, seq_len, head_dim] and
+ * one scale per (lead, token) into args->scale; block_size and zero_point are unused. */
+int fs_quantize_symmetric(const FsQuantizeArgs* a, void* stream) {
+  if (a == nullptr || a->x == nullptr || a->values == nullptr || a->scale == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  if (a->n_lead <= 0 || a->seq_len <= 0 || a->head_dim <= 0) return FS_ERR_INVALID_ARGUMENT;
+  if (a->x_dtype != FS_F16 && a->x_dtype != FS_BF16 && a->x_dtype != FS_F32) return FS_ERR_UNSUPPORTED;
+  const int64_t rows = a->n_lead * a->seq_len;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks >= (1ll << 31)) return FS_ERR_UNSUPPORTED;
+  fsb::quantize_sym_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      a->x, a->x_dtype, rows, a->head_dim, a->values, a->scale);
+  return fsb::launch_status("symmetric quantize kernel launch");
+}
 
 int fs_abi_version(void) { return FS_ABI_VERSION; }
 

@@ -494,3 +494,33 @@ class PagedKVAllocator:
             "capacity_utilization": used / max(1, cap), "padding_waste": float(waste),
             "fragmentation": waste / max(1, at),
         }
+
+
+def paged_cache_symmetric(k: torch.Tensor, v: torch.Tensor, page: int = 16, *, lengths: Optional[torch.Tensor] = None,
+                          perm: Optional[torch.Tensor] = None) -> PagedKVCache:
+    """Dense fp16/bf16 K/V [B, Hkv, S, D] -> a PagedKVCache in the symmetric per-token
+    format (FS_KV_SYMMETRIC): pool values [P, Hkv, page, D] int8 and scales [P, Hkv, page]
+    fp32, P = B * ceil(S / page) pages, physical page perm[j] holding logical page j of
+    the batch-major order (identity when perm is None); the table is the inverse map."""
+    from .quant import quantize_int8_symmetric_per_token
+
+    if k.ndim != 4 or k.shape != v.shape:
+        raise ValueError("k and v must be [batch, heads, seq_len, head_dim] of one shape")
+    b, h, s_, d = (int(x) for x in k.shape)
+    bps = (s_ + page - 1) // page
+    total = b * bps
+    pad = bps * page - s_
+
+    def pool(x):
+        if pad:
+            x = torch.cat([x, x.new_zeros((b, h, pad, d))], dim=2)
+        x = x.reshape(b, h, bps, page, d).permute(0, 2, 1, 3, 4).reshape(total, h, page, d)
+        if perm is not None:
+            x = torch.empty_like(x).index_copy_(0, perm.to(x.device), x)
+        return quantize_int8_symmetric_per_token(x, page)
+
+    table = torch.arange(total, device=k.device).view(b, bps)
+    if perm is not None:
+        table = perm.to(k.device).view(b, bps)
+    lens = torch.full((b,), s_, dtype=torch.int64, device=k.device) if lengths is None else lengths.to(torch.int64)
+    return PagedKVCache(pool(k), pool(v), table, lens, page, s_)

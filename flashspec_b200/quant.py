@@ -95,8 +95,66 @@ def dequantize_int8_per_block(q, dtype: Optional[torch.dtype] = None) -> torch.T
 
 
 def estimate_quantized_bytes(q) -> int:
-    """quant.py:232-247: values + 4*scale + 2*zero_point elements."""
-    return int(q.values.numel() + q.scale.numel() * 4 + q.zero_point.numel() * 2)
+    """quant.py:232-247: values + 4*scale + 2*zero_point elements (no zero points in the
+    symmetric format)."""
+    zp = getattr(q, "zero_point", None)
+    return int(q.values.numel() + q.scale.numel() * 4 + (zp.numel() * 2 if zp is not None else 0))
+
+
+@dataclass
+class SymQuantizedTensor:
+    """Symmetric per-token INT8 (FS_KV_SYMMETRIC): values int8 [..., S_pad, D] =
+    clamp(rint(x / s), -127, 127) with s = max(absmax / 127, 1e-8) per token and head,
+    scale fp32 [..., S_pad]; S_pad = the sequence padded with zero tokens to a multiple
+    of block_size.  No zero points.  The reference has no such format (it lists
+    symmetric INT8 as future work, doc/TODO.MD:241-255); the benchmark configurations'
+    wording describes it."""
+
+    values: torch.Tensor
+    scale: torch.Tensor
+    block_size: int
+    original_shape: Tuple[int, ...]
+    zero_point: Optional[torch.Tensor] = None
+    symmetric: bool = True
+
+    @property
+    def device(self) -> torch.device:
+        return self.values.device
+
+
+def quantize_int8_symmetric_per_token(x: torch.Tensor, block_size: int = 16) -> SymQuantizedTensor:
+    """x [..., S, D] (fp16 / bf16 / fp32, CUDA) -> SymQuantizedTensor; the sequence is
+    zero-padded to a multiple of block_size (padded tokens get scale 1e-8, values 0)."""
+    require_cuda(x, "x")
+    if x.ndim < 2 or x.shape[-1] <= 0 or x.shape[-2] <= 0:
+        raise ValueError("input needs non-empty sequence and feature dimensions")
+    if block_size <= 0:
+        raise ValueError("block_size must be positive")
+    shape = tuple(int(s) for s in x.shape)
+    seq, d = shape[-2], shape[-1]
+    pad = (-seq) % block_size
+    xc = x.detach()
+    if pad:
+        xc = torch.cat([xc, xc.new_zeros((*shape[:-2], pad, d))], dim=-2)
+    xc = xc.contiguous()
+    n_lead = 1
+    for s_ in shape[:-2]:
+        n_lead *= s_
+    values = torch.empty(xc.shape, dtype=torch.int8, device=x.device)
+    scale = torch.empty(xc.shape[:-1], dtype=torch.float32, device=x.device)
+    args = _lib.FsQuantizeArgs(xc.data_ptr(), dtype_code(xc), n_lead, seq + pad, d, block_size, values.data_ptr(),
+                               scale.data_ptr(), None)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().fs_quantize_symmetric(C.byref(args), stream_of(x.device)), "fs_quantize_symmetric")
+    return SymQuantizedTensor(values, scale, block_size, shape)
+
+
+def dequantize_int8_symmetric(q: SymQuantizedTensor, dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """values * scale, back to original_shape."""
+    x = q.values.to(torch.float32) * q.scale.to(torch.float32).unsqueeze(-1)
+    lead, seq, d = tuple(q.original_shape[:-2]), q.original_shape[-2], q.original_shape[-1]
+    x = x.reshape(*lead, -1, d)[..., :seq, :]
+    return x.to(dtype) if dtype is not None else x
 
 
 def build_compression_stats(dense_bytes: float, quant_bytes: float, *, materializes_dense_kv: bool,

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define FS_ABI_VERSION 2
+#define FS_ABI_VERSION 3
 
 typedef enum FsStatus {
   FS_OK = 0,
@@ -47,6 +47,15 @@ typedef enum FsStatus {
 typedef enum FsDtype { FS_F16 = 0, FS_BF16 = 1, FS_F32 = 2 } FsDtype;
 
 typedef enum FsKvLayout { FS_LAYOUT_CONTIGUOUS = 0, FS_LAYOUT_PAGED = 1 } FsKvLayout;
+
+/* KV formats.  FS_KV_AFFINE_BLOCK is the reference's (quant.py:94-165): values int8 =
+ * u - 128, fp32 scale and int16 zero point per [block_size x D] block.
+ * FS_KV_SYMMETRIC (no counterpart in the reference, which lists symmetric INT8 as future
+ * work, doc/TODO.MD:241-255): values int8 = rint(x / s), fp32 scale s = absmax / 127 per
+ * (token, head), no zero points (k_zero / v_zero unused); scales laid out like the values
+ * without the head_dim axis ([P, Hkv, page] paged, [B, Hkv, S] contiguous); runs on the
+ * generic kernel with one page = one block (block_size = page_size <= 64). */
+typedef enum FsKvFormat { FS_KV_AFFINE_BLOCK = 0, FS_KV_SYMMETRIC = 1 } FsKvFormat;
 
 /* Arguments of one decode-attention call (one query token per request). */
 typedef struct FsDecodeArgs {
@@ -86,6 +95,7 @@ typedef struct FsDecodeArgs {
   int32_t q_dtype;            /* FsDtype of q and out: FS_F16 or FS_BF16              */
   int32_t page_size;          /* paged: tokens per page, a multiple of block_size
                                  (0 = block_size); contiguous: ignored                 */
+  int32_t kv_format;          /* FsKvFormat of K and V                                */
 } FsDecodeArgs;
 
 /* Library version / ABI check. */
@@ -198,6 +208,12 @@ typedef struct FsQuantizeArgs {
   int16_t* zero_point;
 } FsQuantizeArgs;
 int fs_quantize_blocks(const FsQuantizeArgs* args, void* stream);
+
+/* Symmetric per-token quantization into the FS_KV_SYMMETRIC format: x [n_lead, seq_len,
+ * head_dim] -> values [n_lead, seq_len, head_dim] (rint(x / s) clamped to [-127, 127])
+ * and scale [n_lead, seq_len] (s = max(absmax / 127, 1e-8)); block_size and zero_point
+ * are unused.  No counterpart in the reference (doc/TODO.MD:241-255 lists it). */
+int fs_quantize_symmetric(const FsQuantizeArgs* args, void* stream);
 
 /* One page rewrite: rows [dst_row, dst_row+n_rows) of physical page `page`
  * take tokens [src_t, src_t+n_rows) of source request src_b; the other rows

@@ -494,6 +494,38 @@ def tree_verify_attention(q: np.ndarray, cache: OPagedCache, tree_k: np.ndarray,
     return out.astype(q.dtype)
 
 
+# ---------------------------------------------------------------------------
+# symmetric per-token INT8 -- the format of the benchmark configurations' wording; the
+# reference lists it as future work (doc/TODO.MD:241-255), so this is the specification
+# restated: s = max(absmax / 127, 1e-8) per (token, head), q = clamp(rint(x / s), +-127)
+# ---------------------------------------------------------------------------
+
+
+def quantize_symmetric(x: np.ndarray):
+    """x [..., S, D] -> (values int8 [..., S, D], scale fp32 [..., S]), each step fp32."""
+    xf = np.asarray(x, F32)
+    s = np.maximum(np.abs(xf).max(-1) / F32(127.0), _SCALE_FLOOR).astype(F32)
+    q = np.clip(np.rint(xf / s[..., None]), -127, 127).astype(np.int8)
+    return q, s
+
+
+def symmetric_paged_attention(q: np.ndarray, k_values: np.ndarray, k_scale: np.ndarray, v_values: np.ndarray,
+                              v_scale: np.ndarray, table: np.ndarray, lengths: np.ndarray, max_seq_len: int) -> np.ndarray:
+    """Paged attention over a symmetric pool (values [P, Hkv, page, D], scales
+    [P, Hkv, page]): dequantize (values * scale), gather by table.clamp_min(0), masked
+    reference attention -- the reference's paged path (attention.py:171-223) with this
+    format's dequantization."""
+    b, cols = table.shape
+    t = np.maximum(table, 0)
+
+    def dense(vals, sc):
+        x = vals.astype(F32) * sc[..., None]  # [P, H, page, D]
+        g = x[t]  # [B, cols, H, page, D]
+        return g.transpose(0, 2, 1, 3, 4).reshape(b, x.shape[1], -1, x.shape[-1])[..., :max_seq_len, :]
+
+    return _gqa_attention(q, dense(k_values, k_scale), dense(v_values, v_scale), lengths)
+
+
 def algorithmic_bytes_paged(batch: int, q_heads: int, kv_heads: int, head_dim: int, lengths: Sequence[int],
                             page: int = 16, table_cols: Optional[int] = None, q_bytes: int = 2) -> int:
     """Algorithmic bytes of one paged decode call: for every referenced (page, kv
