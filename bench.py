@@ -673,8 +673,9 @@ def paged_vs_contiguous(args, wl, timer):
 
 def other_configs(args, timer, dev):
     """cfg0 (contiguous, four rotated input copies), cfg2 (ragged GQA at its configured
-    4 splits and on the default plan) and cfg4 (the serving loop), each on this GPU, so
-    one default run records every configuration's device time."""
+    4 splits and on the default plan), cfg1's shape in the symmetric per-token format, and
+    cfg4 (the serving loop), each on this GPU, so one default run records every
+    configuration's device time."""
     import torch
 
     import flashspec_b200 as fs
@@ -709,6 +710,23 @@ def other_configs(args, timer, dev):
             step2(i)
         line(tag, wl2.bytes_per_call, timer.run(step2, n) / n)
     del wl2
+    torch.cuda.empty_cache()
+
+    # cfg1's shape in the symmetric per-token format of the configurations' wording
+    g = torch.Generator(device=dev).manual_seed(0)
+    b, h, seq, d = 16, 32, 4096, 128
+    k = torch.randn(b, h, seq, d, generator=g, device=dev, dtype=torch.float16)
+    v = torch.randn(b, h, seq, d, generator=g, device=dev, dtype=torch.float16)
+    q = torch.randn(b, h, d, generator=g, device=dev, dtype=torch.float16)
+    perm = torch.randperm(b * seq // 16, generator=torch.Generator().manual_seed(1))
+    sym = fs.paged_cache_symmetric(k, v, 16, perm=perm)
+    del k, v
+    step_s = lambda i: fs.paged_quant_attention_cuda(q, sym)
+    for i in range(8):
+        step_s(i)
+    sym_bytes = b * (seq // 16) * h * 2 * (16 * d + 16 * 4) + 2 * b * h * d * 2 + b * (seq // 16) * 8 + b * 8
+    line("cfg1_symmetric_per_token", sym_bytes, timer.run(step_s, n) / n, kernel="tuned decode kernels, per-token scales")
+    del sym, q
     torch.cuda.empty_cache()
 
     sc = ServingConfig(steps=2000, seed=0)

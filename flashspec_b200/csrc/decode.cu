@@ -47,7 +47,7 @@ constexpr int kD = 128;
 constexpr int kPage = 16;
 constexpr int kPageBytes = kPage * kD;     // 2048
 constexpr int kStageBytes = 2 * kPageBytes;  // K + V
-constexpr int kMetaBytes = 32;
+constexpr int kMetaBytes = 160;  // 32 bytes of page qparams + 128 bytes of per-token scales
 constexpr int kMaxG = 8;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 constexpr uint32_t kProducerSleepNs = 1000;  // suspend hint of the producer's free-stage waits
@@ -77,6 +77,7 @@ struct DecodeParams {
   int tier_ctas, skew;  // balanced kernel: CTAs per tier (the SM count) and the tier weight step
   int piece_cost;       // balanced kernel: virtual pages charged per (request, kv head) pair
   int debug_mode;       // profiling only (FLASHSPEC_DEBUG_MODE)
+  int sym;              // FS_KV_SYMMETRIC: per-token scales [blocks, 16], no zero points
 };
 
 // Shared-memory plan of one CTA: a ring of kNS page stages (K 2 KB + V 2 KB, 1024-byte
@@ -103,11 +104,15 @@ struct SmemLayout {
 
 constexpr uint32_t kMagic = 0x64646464u;  // fp16 exponent bytes: half 0x64xx == 1024 + xx
 
-// qparams of one stage as the consumers read them
+// qparams of one stage as the consumers read them; tok != 0 (symmetric format) is the
+// shared address of the stage's 16 K then 16 V per-token scales
 struct StageInfo {
   float ks, vs;
   uint32_t kz, vz;
+  uint32_t tok;
 };
+
+constexpr uint32_t kStageSym = 4u;  // meta flag: the stage carries per-token scales
 
 // Producer side, one lane: fill stage `st` with the (page, kv head) block whose index in
 // the [blocks, 16, 128] view is `e` (< 0: nothing to load, the stage is marked invalid).
@@ -118,6 +123,18 @@ __device__ __forceinline__ void issue_page(const DecodeParams& p, const CUtensor
   if (e < 0) {
     m[4] = 0u;
     mbar_arrive(full);
+    mbar_arrive(full);
+    return;
+  }
+  if (p.sym) {  // symmetric format: 16 K and 16 V per-token scales, 64 bytes each
+    m[4] = 1u | kStageSym;
+    mbar_arrive_expect_tx(full, kStageBytes + 128);
+    const uint32_t dst = base_s + st * kStageBytes;
+    tma_load_2d(dst, tmk, 0, (int32_t)(e * kPage), full, policy);
+    tma_load_2d(dst + kPageBytes, tmv, 0, (int32_t)(e * kPage), full, policy);
+    const uint32_t ms = meta_s + st * kMetaBytes + 32;
+    bulk_load(ms, p.k_scale + e * kPage, 64, full);
+    bulk_load(ms + 64, p.v_scale + e * kPage, 64, full);
     mbar_arrive(full);
     return;
   }
@@ -161,10 +178,17 @@ __device__ __forceinline__ int64_t block_index(const DecodeParams& p, int b, int
   return ((int64_t)b * p.Hkv + h) * p.num_blocks + phys;
 }
 
-__device__ __forceinline__ bool read_stage_info(const uint32_t* meta_p, int st, StageInfo& si) {
+__device__ __forceinline__ bool read_stage_info(const uint32_t* meta_p, int st, StageInfo& si, uint32_t meta_s) {
   const volatile uint32_t* m = meta_p + st * (kMetaBytes / 4);
   const uint32_t flags = m[4];
   if (!(flags & 1u)) return false;
+  if (flags & kStageSym) {  // stored values are the signed integers: zero point 128 in the u domain
+    si.ks = si.vs = 1.f;
+    si.kz = si.vz = 128u;
+    si.tok = meta_s + st * kMetaBytes + 32;
+    return true;
+  }
+  si.tok = 0u;
   si.ks = __uint_as_float(m[0]);
   si.vs = __uint_as_float(m[1]);
   const uint32_t sh = (flags & 2u) ? 16u : 0u;
@@ -340,11 +364,25 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
   }
   const float f = si.ks * qf.qscale * qk_scale_log2;
   const int zc = (128 - (int)si.kz) * qf.q16sum;
+  // per-token scales of this thread's tokens 2c, 2c+1, 8+2c, 9+2c (symmetric format)
+  float fk[4] = {f, f, f, f}, vk[4] = {si.vs, si.vs, si.vs, si.vs};
+  if (si.tok != 0u) {
+    const float2 k01 = lds64f(si.tok + 8 * c), k89 = lds64f(si.tok + 32 + 8 * c);
+    const float2 v01 = lds64f(si.tok + 64 + 8 * c), v89 = lds64f(si.tok + 96 + 8 * c);
+    fk[0] = f * k01.x;
+    fk[1] = f * k01.y;
+    fk[2] = f * k89.x;
+    fk[3] = f * k89.y;
+    vk[0] = v01.x;
+    vk[1] = v01.y;
+    vk[2] = v89.x;
+    vk[3] = v89.y;
+  }
   float t[4];
-  t[0] = (float)((shi[0][0] << 8) + slo[0][0] + zc) * f;  // token 2c
-  t[1] = (float)((shi[0][1] << 8) + slo[0][1] + zc) * f;  // token 2c+1
-  t[2] = (float)((shi[1][0] << 8) + slo[1][0] + zc) * f;  // token 8+2c
-  t[3] = (float)((shi[1][1] << 8) + slo[1][1] + zc) * f;  // token 9+2c
+  t[0] = (float)((shi[0][0] << 8) + slo[0][0] + zc) * fk[0];  // token 2c
+  t[1] = (float)((shi[0][1] << 8) + slo[0][1] + zc) * fk[1];  // token 2c+1
+  t[2] = (float)((shi[1][0] << 8) + slo[1][0] + zc) * fk[2];  // token 8+2c
+  t[3] = (float)((shi[1][1] << 8) + slo[1][1] + zc) * fk[3];  // token 9+2c
   if (pos0 + kPage > len_eff) {
     if (pos0 + 2 * c >= len_eff) t[0] = -INFINITY;
     if (pos0 + 2 * c + 1 >= len_eff) t[1] = -INFINITY;
@@ -374,8 +412,8 @@ __device__ __forceinline__ void consume_page(uint32_t sbase, const StageOffsets&
 #pragma unroll
   for (int k = 0; k < 4; ++k) pr[k] = ex2_approx(t[k] - ws.m_run);
   ws.l_run += (pr[0] + pr[1]) + (pr[2] + pr[3]);
-  const uint32_t pb0 = pack_half2(pr[0] * si.vs, pr[1] * si.vs);
-  const uint32_t pb1 = pack_half2(pr[2] * si.vs, pr[3] * si.vs);
+  const uint32_t pb0 = pack_half2(pr[0] * vk[0], pr[1] * vk[1]);
+  const uint32_t pb1 = pack_half2(pr[2] * vk[2], pr[3] * vk[3]);
   {  // the zero point, applied per page to the exact fp16 P values the MMAs see
     const float2 p01 = __half22float2(*reinterpret_cast<const __half2*>(&pb0));
     const float2 p23 = __half22float2(*reinterpret_cast<const __half2*>(&pb1));
@@ -514,7 +552,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
         break;
       }
       StageInfo si;
-      if (kMode == 2 || !read_stage_info(meta_p, st, si)) {  // masked page (or data-only profiling)
+      if (kMode == 2 || !read_stage_info(meta_p, st, si, meta_s)) {  // masked page (or data-only profiling)
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_s + 8 * st);
         continue;
@@ -1037,7 +1075,7 @@ __global__ void __maxnreg__(kMaxRegs)
     }
     if (j == 0) trace_mark<kTrace>(p, kW + 1, lane, 2);
     StageInfo si;
-    if (read_stage_info(meta_p, st, si) && p.debug_mode != 2 && p.debug_mode != 4) {
+    if (read_stage_info(meta_p, st, si, meta_s) && p.debug_mode != 2 && p.debug_mode != 4) {
       consume_page<0>(base_s + st * kStageBytes, off, empty_s + 8 * st, lane, si, qf, p.qk_scale_log2,
                       (lo + (int)(f - pair_P)) * kPage, len_eff, ws);
     } else {
@@ -1452,7 +1490,7 @@ static size_t workspace_for(const FsDecodeArgs* a, int splits) {
 
 // The shapes of the tuned TMA kernels: D = 128, pages = quant blocks = 16 tokens, fp16 q.
 static bool tuned_shape(const FsDecodeArgs* a) {
-  return a->kv_format == FS_KV_AFFINE_BLOCK && a->head_dim == kD && a->block_size == kPage && (a->page_size == 0 || a->page_size == kPage) &&
+  return a->head_dim == kD && a->block_size == kPage && (a->page_size == 0 || a->page_size == kPage) &&
          a->q_dtype == FS_F16;
 }
 
@@ -1489,6 +1527,10 @@ static int validate(const FsDecodeArgs* a, int layout) {
     return FS_ERR_ALIGNMENT;
   if ((reinterpret_cast<uintptr_t>(a->k_zero) | reinterpret_cast<uintptr_t>(a->v_zero) |
        reinterpret_cast<uintptr_t>(a->k_scale) | reinterpret_cast<uintptr_t>(a->v_scale)) & 3)
+    return FS_ERR_ALIGNMENT;
+  // the symmetric format's per-token scales travel as 64-byte bulk copies
+  if (a->kv_format == FS_KV_SYMMETRIC &&
+      ((reinterpret_cast<uintptr_t>(a->k_scale) | reinterpret_cast<uintptr_t>(a->v_scale)) & 15))
     return FS_ERR_ALIGNMENT;
   return FS_OK;
 }
@@ -1544,6 +1586,7 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.skew = tier_skew();
   p.piece_cost = piece_cost();
   p.debug_mode = debug_mode();
+  p.sym = a->kv_format == FS_KV_SYMMETRIC;
   if (need > 0) {
     const size_t G = (size_t)p.G;
     const size_t units = pl.balanced ? (size_t)pl.ctas * kShapes[shape].warps * 2 * G

@@ -53,8 +53,10 @@ typedef enum FsKvLayout { FS_LAYOUT_CONTIGUOUS = 0, FS_LAYOUT_PAGED = 1 } FsKvLa
  * FS_KV_SYMMETRIC (no counterpart in the reference, which lists symmetric INT8 as future
  * work, doc/TODO.MD:241-255): values int8 = rint(x / s), fp32 scale s = absmax / 127 per
  * (token, head), no zero points (k_zero / v_zero unused); scales laid out like the values
- * without the head_dim axis ([P, Hkv, page] paged, [B, Hkv, S] contiguous); runs on the
- * generic kernel with one page = one block (block_size = page_size <= 64). */
+ * without the head_dim axis ([P, Hkv, page] paged, [B, Hkv, S] contiguous), 16-byte
+ * aligned; one page = one block (block_size = page_size <= 64).  D = 128 with 16-token
+ * pages and fp16 q runs the tuned kernels (the stage carries the page's 2 x 64 bytes of
+ * token scales), every other shape the generic kernel. */
 typedef enum FsKvFormat { FS_KV_AFFINE_BLOCK = 0, FS_KV_SYMMETRIC = 1 } FsKvFormat;
 
 /* Arguments of one decode-attention call (one query token per request). */
