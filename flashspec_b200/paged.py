@@ -31,9 +31,38 @@ assert ITEM_DTYPE.itemsize == C.sizeof(_lib.FsPageUpdate)
 _SCALE_FLOOR = float(np.float32(1.0e-8))
 
 
+class _PinnedRing:
+    """Reusable pinned staging buffers for small per-step uploads (page-update items,
+    table changes): a buffer is refilled only after the copy that last read it has
+    completed on the GPU, so no pinned allocation happens per call."""
+
+    def __init__(self, n: int = 8):
+        self.bufs = [None] * n
+        self.events = [None] * n
+        self.i = 0
+
+    def upload(self, arr: np.ndarray, device: torch.device) -> torch.Tensor:
+        raw = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
+        k = self.i
+        self.i = (self.i + 1) % len(self.bufs)
+        if self.events[k] is not None:
+            self.events[k].synchronize()
+        if self.bufs[k] is None or self.bufs[k].numel() < raw.size:
+            self.bufs[k] = torch.empty(max(raw.size, 4096), dtype=torch.uint8).pin_memory()
+        host = self.bufs[k][: raw.size]
+        host.numpy()[:] = raw
+        dev = host.to(device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(device))
+        self.events[k] = ev
+        return dev
+
+
+_RING = _PinnedRing()
+
+
 def _upload(arr: np.ndarray, device: torch.device) -> torch.Tensor:
-    host = torch.from_numpy(np.ascontiguousarray(arr).view(np.uint8).reshape(-1))
-    return host.pin_memory().to(device, non_blocking=True)
+    return _RING.upload(arr, device)
 
 
 def page_update(items: np.ndarray, k_src: torch.Tensor, v_src: torch.Tensor, dst_k: QuantizedTensor,
@@ -318,6 +347,12 @@ class PagedKVAllocator:
         self._npages = np.zeros(16, np.int64)
         self._lens = np.zeros(16, np.int64)
         self._free_slots: List[int] = list(range(16))
+        # device copy of the slot-indexed table and lengths, updated by the changes since
+        # the last to_cache (entries (slot, col) and slots whose length changed)
+        self._dtab: Optional[torch.Tensor] = None
+        self._dlens: Optional[torch.Tensor] = None
+        self._dirty_e: List[Tuple[np.ndarray, np.ndarray]] = []
+        self._dirty_l: List[np.ndarray] = []
 
     # -- bookkeeping ----------------------------------------------------------------
     @property
@@ -393,6 +428,8 @@ class PagedKVAllocator:
         self._ptab[slot, :need] = pages
         self._npages[slot] = need
         self._lens[slot] = eff
+        self._dirty_e.append((np.full(need, slot, np.int64), np.arange(need, dtype=np.int64)))
+        self._dirty_l.append(np.array([slot], np.int64))
         if need:
             items = np.zeros(need, ITEM_DTYPE)
             starts = np.arange(need) * self.block_size
@@ -427,8 +464,11 @@ class PagedKVAllocator:
         if t == 1:  # decode step: one row into each tail page
             off = lens % bs
             lb = lens // bs
-            for i in np.nonzero(need_pages)[0]:  # new tail pages, lowest free first, request order
+            grown = np.nonzero(need_pages)[0]
+            for i in grown:  # new tail pages, lowest free first, request order
                 self._ptab[slots[i], lb[i]] = self._allocate_block()
+            if len(grown):
+                self._dirty_e.append((slots[grown].astype(np.int64), lb[grown].astype(np.int64)))
             self._npages[slots] = np.maximum(npg, lb + 1)
             items = np.zeros(len(ids), ITEM_DTYPE)
             items["page"] = self._ptab[slots, lb]
@@ -444,11 +484,13 @@ class PagedKVAllocator:
                     if lb_ == self._npages[slot]:
                         self._ptab[slot, lb_] = self._allocate_block()
                         self._npages[slot] += 1
+                        self._dirty_e.append((np.array([slot], np.int64), np.array([lb_], np.int64)))
                     n = min(t - ti, bs - off_)
                     recs.append((int(self._ptab[slot, lb_]), bi, ti, off_, n, 0, 0))
                     ti += n
             items = np.array(recs, ITEM_DTYPE)
         self._lens[slots] += t
+        self._dirty_l.append(slots.astype(np.int64))
         for r in reqs:
             r.length += t
         page_update(items, k_new, v_new, self.k_quant, self.v_quant)
@@ -458,6 +500,9 @@ class PagedKVAllocator:
         req = self._requests.pop(int(request_id))
         for p in self._ptab[req.slot, : self._npages[req.slot]].tolist():
             heapq.heappush(self._free, p)
+        n_old = int(self._npages[req.slot])
+        self._dirty_e.append((np.full(n_old, req.slot, np.int64), np.arange(n_old, dtype=np.int64)))
+        self._dirty_l.append(np.array([req.slot], np.int64))
         self._ptab[req.slot, :] = -1
         self._npages[req.slot] = 0
         self._lens[req.slot] = 0
@@ -470,15 +515,45 @@ class PagedKVAllocator:
         return self._ptab[slots, :cols].copy(), self._lens[slots].copy()
 
     def to_cache(self, request_ids: Optional[Sequence[int]] = None) -> PagedKVCache:
-        """paged.py:153-179: table/lengths in the given request order, -1 padded."""
+        """paged.py:153-179: table/lengths in the given request order, -1 padded.
+
+        The slot-indexed table and lengths live on the device; a call uploads only what
+        changed since the previous one (new page entries, entries of released requests
+        reset to -1, changed lengths) together with the batch's slot list, in one pinned
+        copy, and gathers the batch's rows on the device.  The first call, and any call
+        after the host table grew, uploads the whole table."""
         ids = self.live_request_ids if request_ids is None else [int(r) for r in request_ids]
         if not ids:
             raise ValueError("to_cache needs at least one live request")
-        table, lens = self.block_table_numpy(ids)
-        packed = np.concatenate([lens, table.reshape(-1)])
-        dev = _upload(packed, self.device).view(torch.int64)
-        return PagedKVCache(self.k_quant, self.v_quant, dev[len(ids):].view(len(ids), -1), dev[: len(ids)],
-                            self.block_size, int(lens.max()))
+        slots = np.fromiter((self._get(r).slot for r in ids), np.int64, len(ids))
+        cols = max(1, int(self._npages[slots].max()))
+        max_len = int(self._lens[slots].max())
+        b = len(ids)
+        if self._dtab is None or tuple(self._dtab.shape) != self._ptab.shape:
+            packed = np.concatenate([self._lens, self._ptab.reshape(-1), slots])
+            dev = _upload(packed, self.device).view(torch.int64)
+            rows = self._ptab.shape[0]
+            self._dlens = dev[:rows].clone()
+            self._dtab = dev[rows: rows + self._ptab.size].view(self._ptab.shape).clone()
+            slots_dev = dev[rows + self._ptab.size:]
+        else:
+            es = np.concatenate([e[0] for e in self._dirty_e]) if self._dirty_e else np.zeros(0, np.int64)
+            ec = np.concatenate([e[1] for e in self._dirty_e]) if self._dirty_e else np.zeros(0, np.int64)
+            ls = np.unique(np.concatenate(self._dirty_l)) if self._dirty_l else np.zeros(0, np.int64)
+            ne, nl = es.size, ls.size
+            packed = np.concatenate([es, ec, self._ptab[es, ec], ls, self._lens[ls], slots])
+            dev = _upload(packed, self.device).view(torch.int64)
+            if ne:
+                self._dtab.index_put_((dev[:ne], dev[ne:2 * ne]), dev[2 * ne:3 * ne])
+            if nl:
+                self._dlens.index_put_((dev[3 * ne:3 * ne + nl],), dev[3 * ne + nl:3 * ne + 2 * nl])
+            slots_dev = dev[3 * ne + 2 * nl:]
+        self._dirty_e.clear()
+        self._dirty_l.clear()
+        table = self._dtab[:, :cols].index_select(0, slots_dev)
+        lengths = self._dlens.index_select(0, slots_dev)
+        assert table.shape == (b, cols)
+        return PagedKVCache(self.k_quant, self.v_quant, table, lengths, self.block_size, max_len)
 
     def stats(self) -> Dict[str, float]:
         """paged.py:181-199."""

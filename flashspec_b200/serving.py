@@ -107,6 +107,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
         sched.arrivals()
         p0 = ev()
         p0.record()
+        admitted_before = admitted
         while sched.queue and len(live) < cfg.max_live:
             r = sched.queue[0]
             need = _pages(r.prompt + r.out_len, cfg.page)
@@ -166,9 +167,13 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
         s1 = ev()
         s1.record()
         if measure:  # read after the loop: no host synchronisation inside it
-            marks.append((s0, s1, p0, p1, a0, a1, t0, t1))
+            marks.append((s0, s1, p0, p1, a0, a1, t0, t1, admitted - admitted_before))
     torch.cuda.synchronize(device)
-    for s0, s1, p0, p1, a0, a1, t0, t1 in marks:
+    ttft_sum, ttft_n = 0.0, 0
+    for s0, s1, p0, p1, a0, a1, t0, t1, n_adm in marks:
+        if n_adm:  # a request admitted in this step gets its first token at the step's attention
+            ttft_sum += n_adm * p0.elapsed_time(t1)
+            ttft_n += n_adm
         t_attn += t0.elapsed_time(t1)
         t_append += a0.elapsed_time(a1)
         t_prefill += p0.elapsed_time(p1)
@@ -193,6 +198,7 @@ def run(cfg: ServingConfig, device="cuda", measure: bool = True, recorder: Optio
             "attention_bytes": attn_bytes, "append_bytes": append_bytes,
             "tokens_per_s_device": tokens / (sum(step_times) * 1e-3),
             "steps_measured": len(step_times), "gpu_launches": launches,
+            "ttft_ms_mean": ttft_sum / max(1, ttft_n), "tpot_ms": float(np.mean(step_times)),
         })
     return res
 
@@ -209,3 +215,147 @@ def main(argv=None):
 
 if __name__ == "__main__":
     main()
+
+
+# ------------------------------------------------------------------------------------
+# The reference's serving simulation API on the GPU allocator
+# ------------------------------------------------------------------------------------
+
+
+@dataclass(frozen=True)
+class SimulationConfig:
+    """The fields and defaults of the reference's serving ``ServingConfig``
+    (src/flashspec/serving.py:15-30); device is a CUDA device here."""
+
+    requests: int = 8
+    prompt_len: int = 128
+    prompt_lens: Optional[tuple] = None
+    prompt_length_distribution: str = "uniform"
+    decode_steps: int = 16
+    request_life_steps: int = 0
+    heads: int = 8
+    head_dim: int = 64
+    block_size: int = 16
+    allocator_blocks: Optional[int] = None
+    seed: int = 0
+    device: str = "cuda"
+    dtype: str = "auto"
+
+
+def _sim_dtype(name: str) -> torch.dtype:
+    n = name.strip().lower()
+    if n in ("auto", "float16", "fp16"):
+        return torch.float16
+    if n in ("bfloat16", "bf16"):
+        return torch.bfloat16
+    raise ValueError("dtype must be auto, float16 or bfloat16 (the CUDA decode takes fp16 / bf16 q)")
+
+
+def run_decode_simulation(config: SimulationConfig) -> Dict[str, object]:
+    """The reference's deterministic serving simulation (src/flashspec/serving.py:33-190)
+    with the same steps, prompt-length sampling, allocator sizing and result keys, on
+    this package's device allocator and CUDA decode: prefill of ``requests`` requests, the
+    first decode attention (TTFT = prefill + first attention), then ``decode_steps``
+    steps of attention + append of one token per request (K = out, V = tanh(out), as the
+    reference derives them), with optional finish / arrival every ``request_life_steps``.
+    Times are host wall clock around synchronised regions, as in the reference."""
+    import flashspec_b200 as fs
+
+    if config.requests <= 0 or config.prompt_len <= 0:
+        raise ValueError("requests and prompt_len must be positive")
+    if config.decode_steps < 0 or config.request_life_steps < 0:
+        raise ValueError("decode_steps and request_life_steps must not be negative")
+    if config.heads <= 0 or config.head_dim <= 0 or config.block_size <= 0:
+        raise ValueError("heads, head_dim and block_size must be positive")
+    device = torch.device(config.device)
+    if device.type != "cuda":
+        raise RuntimeError("the simulation runs on a CUDA device")
+    dtype = _sim_dtype(config.dtype)
+    gen = torch.Generator(device=device).manual_seed(config.seed)
+    lens = tuple(int(x) for x in (config.prompt_lens if config.prompt_lens is not None else (config.prompt_len,)))
+    if not lens or any(x <= 0 for x in lens):
+        raise ValueError("prompt_lens must be positive")
+    if config.allocator_blocks is not None:
+        capacity = int(config.allocator_blocks)
+    else:
+        per_live = max(lens) + max(1, config.decode_steps)
+        capacity = max(1, config.requests * ((per_live + config.block_size - 1) // config.block_size))
+    alloc = fs.PagedKVAllocator(capacity_blocks=capacity, heads=config.heads, head_dim=config.head_dim,
+                                block_size=config.block_size, device=device)
+    mode = config.prompt_length_distribution.strip().lower()
+    if mode not in ("uniform", "cycle", "random", "bimodal"):
+        raise ValueError("prompt_length_distribution must be uniform, random or bimodal")
+
+    def sample_len(i: int) -> int:
+        if mode in ("uniform", "cycle"):
+            return lens[i % len(lens)]
+        if mode == "random":
+            return lens[int(torch.randint(len(lens), (1,), generator=gen, device=device).item())]
+        return lens[0] if (len(lens) == 1 or i % 2 == 0) else lens[-1]
+
+    state = {"next": 0, "prefill_ms": 0.0, "arrival_prefill_ms": 0.0, "arrivals": 0}
+    active: List[int] = []
+    generated: Dict[int, int] = {}
+    prompt_of: Dict[int, int] = {}
+
+    def add(initial: bool) -> int:
+        rid = state["next"]
+        state["next"] += 1
+        n = sample_len(rid)
+        k = torch.randn((1, config.heads, n, config.head_dim), generator=gen, device=device, dtype=dtype)
+        v = torch.randn((1, config.heads, n, config.head_dim), generator=gen, device=device, dtype=dtype)
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        alloc.add_request(rid, k, v)
+        torch.cuda.synchronize(device)
+        state["prefill_ms" if initial else "arrival_prefill_ms"] += (time.perf_counter() - t0) * 1e3
+        state["arrivals"] += 1
+        generated[rid] = 0
+        prompt_of[rid] = n
+        return rid
+
+    for _ in range(config.requests):
+        active.append(add(True))
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    q = torch.randn((len(active), config.heads, config.head_dim), generator=gen, device=device, dtype=dtype)
+    fs.paged_quant_attention_cuda(q, alloc.to_cache(active))
+    torch.cuda.synchronize(device)
+    first_ms = (time.perf_counter() - t0) * 1e3
+    decode_ms, tokens, finishes = 0.0, 0, 0
+    for _ in range(config.decode_steps):
+        if not active:
+            break
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        q = torch.randn((len(active), config.heads, config.head_dim), generator=gen, device=device, dtype=dtype)
+        out = fs.paged_quant_attention_cuda(q, alloc.to_cache(active))
+        alloc.append_batch(active, out.unsqueeze(2).to(dtype), torch.tanh(out).unsqueeze(2).to(dtype))
+        torch.cuda.synchronize(device)
+        decode_ms += (time.perf_counter() - t0) * 1e3
+        for rid in active:
+            generated[rid] += 1
+        tokens += len(active)
+        if config.request_life_steps > 0:
+            done = [rid for rid in active if generated[rid] >= config.request_life_steps]
+            for rid in done:
+                alloc.release_request(rid)
+                active.remove(rid)
+                generated.pop(rid, None)
+                finishes += 1
+            for _ in done:
+                active.append(add(False))
+    st = alloc.stats()
+    return {
+        "device": str(device), "device_name": torch.cuda.get_device_name(device),
+        "dtype": str(dtype).replace("torch.", ""), "requests": config.requests, "prompt_len": config.prompt_len,
+        "prompt_lens": list(lens), "prompt_length_distribution": config.prompt_length_distribution,
+        "average_prompt_len": sum(prompt_of.values()) / max(1, len(prompt_of)),
+        "decode_steps": config.decode_steps, "request_life_steps": config.request_life_steps,
+        "arrivals": state["arrivals"], "finishes": finishes, "prefill_ms": state["prefill_ms"],
+        "arrival_prefill_ms": state["arrival_prefill_ms"],
+        "total_prefill_ms": state["prefill_ms"] + state["arrival_prefill_ms"], "first_attention_ms": first_ms,
+        "decode_ms": decode_ms, "ttft_ms": state["prefill_ms"] + first_ms,
+        "tpot_ms": decode_ms / max(1, config.decode_steps),
+        "tokens_per_second": tokens / max(1.0e-9, decode_ms / 1000.0), "generated_tokens": tokens, **st,
+    }
