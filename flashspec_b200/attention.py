@@ -26,6 +26,10 @@ PAGE_TOKENS = 16  # tokens per kernel step (one page / quant block)
 NUM_WARPS = 4
 _workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
 _tickets: Dict[Tuple[int, int], torch.Tensor] = {}
+_plans: Dict[tuple, Tuple[int, int]] = {}
+# environment knobs the library's plan reads (decode.cu): part of the plan cache key
+_PLAN_KNOBS = ("FLASHSPEC_DECODE_KERNEL", "FLASHSPEC_KERNEL_SHAPE", "FLASHSPEC_NUM_WARPS", "FLASHSPEC_TIER_SKEW",
+               "FLASHSPEC_PIECE_COST")
 
 
 def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
@@ -98,9 +102,21 @@ def _run(entry: str, args: _lib.FsDecodeArgs, device: torch.device, splits_hint:
     lib = _lib.load()
     stream = stream_of(device)
     args.num_splits = splits_hint
-    nbytes = C.c_size_t(0)
-    splits = C.c_int32(0)
-    _lib.check(lib.fs_decode_workspace_size(C.byref(args), C.byref(nbytes), C.byref(splits)), entry)
+    # the plan (workspace bytes, splits) depends on the shape fields and the env knobs
+    key = (device.index, args.layout, args.batch, args.q_heads, args.kv_heads, args.head_dim, args.block_size,
+           args.page_size, args.num_blocks, args.table_cols, args.max_seq_len, args.num_splits, args.page_begin,
+           args.page_end, bool(args.shard_o), args.q_dtype, args.kv_format,
+           tuple(os.environ.get(k) for k in _PLAN_KNOBS))
+    plan = _plans.get(key)
+    if plan is None:
+        nbytes = C.c_size_t(0)
+        splits = C.c_int32(0)
+        _lib.check(lib.fs_decode_workspace_size(C.byref(args), C.byref(nbytes), C.byref(splits)), entry)
+        plan = _plans[key] = (nbytes.value, splits.value)
+        if len(_plans) > 256:
+            _plans.pop(next(iter(_plans)))
+    nbytes = C.c_size_t(plan[0])
+    splits = C.c_int32(plan[1])
     if nbytes.value:
         ws = _workspace(device, stream, nbytes.value)
         args.workspace = ws.data_ptr()

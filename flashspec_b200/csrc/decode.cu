@@ -1332,6 +1332,34 @@ static int make_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
   return r == CUDA_SUCCESS ? FS_OK : fail_cuda("cuTensorMapEncodeTiled", r);
 }
 
+// Tensor maps depend only on the base address and the row count (box, swizzle and
+// strides are fixed), so the last few are kept: a serving loop calls with the same
+// pools every step and saves the driver's encode.
+static int cached_kv_map(CUtensorMap* map, const void* base, uint64_t rows) {
+  struct Entry {
+    const void* base;
+    uint64_t rows;
+    CUtensorMap map;
+  };
+  static Entry cache[16] = {};
+  static int next = 0;
+  static std::mutex mu;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& e : cache)
+      if (e.base == base && e.rows == rows && base != nullptr) {
+        *map = e.map;
+        return FS_OK;
+      }
+  }
+  const int st = make_kv_map(map, base, rows);
+  if (st != FS_OK) return st;
+  std::lock_guard<std::mutex> lock(mu);
+  cache[next] = Entry{base, rows, *map};
+  next = (next + 1) % 16;
+  return FS_OK;
+}
+
 static int64_t max_pages_of(const FsDecodeArgs* a) {
   int64_t np = ((int64_t)a->max_seq_len + kPage - 1) / kPage;
   if (a->layout == FS_LAYOUT_PAGED)
@@ -1554,8 +1582,8 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   const uint64_t rows = kPaged ? (uint64_t)a->num_blocks * a->kv_heads * kPage
                                : (uint64_t)a->batch * a->kv_heads * a->num_blocks * kPage;
   CUtensorMap tmk, tmv;
-  if ((st = make_kv_map(&tmk, a->k_values, rows)) != FS_OK) return st;
-  if ((st = make_kv_map(&tmv, a->v_values, rows)) != FS_OK) return st;
+  if ((st = cached_kv_map(&tmk, a->k_values, rows)) != FS_OK) return st;
+  if ((st = cached_kv_map(&tmv, a->v_values, rows)) != FS_OK) return st;
 
   DecodeParams p{};
   p.q = reinterpret_cast<const __half*>(a->q);
