@@ -79,6 +79,37 @@ def test_quantize_random_bf16_and_odd_shapes_vs_oracle():
         same_quant(q, O.quantize_int8_per_block(xt.float().cpu().numpy(), bs))
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape,bs", [((4, 8, 1000, 128), 16), ((2, 4, 300, 64), 8), ((2, 3, 640, 256), 32),
+                                      ((3, 2, 100, 32), 16)])
+def test_quantize_vector_kernel_bit_identical_to_division(monkeypatch, dtype, shape, bs):
+    """The 16-byte-per-thread quantizer (reciprocal product, division only near a rounding
+    boundary) against the per-element division kernel (FLASHSPEC_PAGE_UPDATE_SCALAR), on
+    ~4M values of scales 1e-3 .. 1e3 with offsets, ragged tails and a misaligned source."""
+    rng = np.random.default_rng(hash((shape, bs)) % 2**32)
+    n = int(np.prod(shape))
+    x = rng.standard_normal(n).astype(np.float32) * np.repeat(10.0 ** rng.uniform(-3, 3, n // shape[-1]), shape[-1])
+    x += np.repeat(rng.standard_normal(n // shape[-1]) * 5, shape[-1])
+    flat = torch.empty(n + 3, dtype=dtype, device="cuda")
+    flat[3:] = dev(x).to(dtype)
+    xt = flat[3:].view(shape)  # 3 elements off the allocation: misaligned rows take scalar loads
+    outs = []
+    for scalar in (False, True):
+        if scalar:
+            monkeypatch.setenv("FLASHSPEC_PAGE_UPDATE_SCALAR", "1")
+        q = fs().quantize_int8_per_block(xt, bs)
+        q2 = fs().quantize_int8_per_block(xt.contiguous().clone(), bs)
+        torch.cuda.synchronize()
+        outs.append((q, q2))
+    (a, a2), (b, b2) = outs
+    for x1, x2 in ((a, b), (a2, b2), (a, a2)):
+        assert torch.equal(x1.values, x2.values)
+        assert torch.equal(x1.scale, x2.scale)
+        assert torch.equal(x1.zero_point, x2.zero_point)
+    small = xt[:1, :1].float().cpu().numpy()
+    same_quant(fs().quantize_int8_per_block(xt[:1, :1].contiguous(), bs), O.quantize_int8_per_block(small, bs))
+
+
 # ---------------------------------------------------------------------------------
 # contiguous backend
 # ---------------------------------------------------------------------------------
@@ -382,12 +413,16 @@ def test_allocator_lifecycle_bit_exact():
     close(out, g["out"])
 
 
-def test_allocator_random_decode_loop_matches_oracle():
-    rng = np.random.default_rng(11)
+@pytest.mark.parametrize("D,bs", [(128, 16),   # the serving shape: register-resident page update
+                                  (64, 8),     # E = 512, the smallest vector block
+                                  (256, 32),   # E = 8192
+                                  (32, 8)])    # E = 256: the shared-memory page update
+def test_allocator_random_decode_loop_matches_oracle(D, bs):
+    rng = np.random.default_rng(11 + D + bs)
     f = fs()
-    H, D, cap = 4, 128, 64
-    ga = f.PagedKVAllocator(capacity_blocks=cap, heads=H, head_dim=D, device="cuda")
-    oa = O.OAllocator(cap, H, D)
+    H, cap = 4, 64
+    ga = f.PagedKVAllocator(capacity_blocks=cap, heads=H, head_dim=D, block_size=bs, device="cuda")
+    oa = O.OAllocator(cap, H, D, bs)
     live = []
     nxt = 0
     for step in range(60):
@@ -395,7 +430,7 @@ def test_allocator_random_decode_loop_matches_oracle():
             n = int(rng.integers(1, 70))
             k = rng.standard_normal((1, H, n, D)).astype(np.float16)
             v = rng.standard_normal((1, H, n, D)).astype(np.float16)
-            if len(oa.free_blocks) >= (n + 15) // 16 + 8:
+            if len(oa.free_blocks) >= (n + bs - 1) // bs + 8:
                 ga.add_request(nxt, dev(k), dev(v))
                 oa.add_request(nxt, k, v)
                 live.append(nxt)
@@ -416,6 +451,44 @@ def test_allocator_random_decode_loop_matches_oracle():
     if live:
         q = rng.standard_normal((len(live), H, D)).astype(np.float16)
         close(f.paged_quant_attention_cuda(dev(q), ga.to_cache(live)), O.paged_quant_attention(q, oa.to_cache(live)))
+
+
+@pytest.mark.parametrize("D,bs,chunks", [(128, 16, "1"), (128, 16, "2"), (128, 16, "4"), (64, 64, "2"),
+                                         (64, 8, "2")])
+def test_page_update_vector_and_scalar_kernels_bit_identical(monkeypatch, D, bs, chunks):
+    """The same prefill + append + reuse sequence through the register-resident page
+    update (whose quantizer replaces the division by a reciprocal product except near a
+    rounding boundary) and through the shared-memory one with the plain correctly
+    rounded division (forced by FLASHSPEC_PAGE_UPDATE_SCALAR): identical bytes, scales and
+    zero points, for fp16, bf16 and fp32 token sources and value ranges from 1e-3 to 1e3
+    (about 4M quantized elements, a few thousand of them near a half-integer)."""
+    rng = np.random.default_rng(21)
+    f = fs()
+    H, cap = 4, 700
+    pools = []
+    for scalar in (False, True):
+        monkeypatch.setenv("FLASHSPEC_PAGE_UPDATE_CHUNKS", chunks)
+        if scalar:
+            monkeypatch.setenv("FLASHSPEC_PAGE_UPDATE_SCALAR", "1")
+        r = np.random.default_rng(21)
+        a = f.PagedKVAllocator(capacity_blocks=cap, heads=H, head_dim=D, block_size=bs, device="cuda")
+        sizes = [(37, torch.float16, 3.0), (16, torch.bfloat16, 1e-3), (90, torch.float32, 1e3),
+                 (64 * bs, torch.float32, 1.0), (64 * bs + 5, torch.float16, 30.0)]
+        for i, (n, dt, sc) in enumerate(sizes):
+            off = r.standard_normal((1, H, 1, D)).astype(np.float32) * sc
+            k = torch.from_numpy(r.standard_normal((1, H, n, D)).astype(np.float32) * sc + off).to(dt)
+            v = torch.from_numpy(r.standard_normal((1, H, n, D)).astype(np.float32) * sc).to(dt)
+            a.add_request(i, k.cuda(), v.cuda())
+        for _ in range(20):
+            k = torch.from_numpy(r.standard_normal((len(sizes), H, 1, D)).astype(np.float16)).cuda()
+            a.append_batch(list(range(len(sizes))), k, k * 0.5)
+        a.release_request(1)
+        a.add_request(9, k[:1].repeat(1, 1, 5, 1), k[:1].repeat(1, 1, 5, 1))
+        torch.cuda.synchronize()
+        pools.append([t.clone() for qt in (a.k_quant, a.v_quant) for t in (qt.values, qt.scale, qt.zero_point)])
+        monkeypatch.delenv("FLASHSPEC_PAGE_UPDATE_SCALAR", raising=False)
+    for x, y in zip(*pools):
+        assert torch.equal(x, y)
 
 
 # ---------------------------------------------------------------------------------
