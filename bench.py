@@ -525,7 +525,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         def make_run(b, views):
             c = fs.PagedKVCache(cache.k_quant, cache.v_quant, views[1], views[2], cache.block_size,
                                 cache.max_seq_len)
-            if seqshard:  # one captured decoder step (decode + exchange) per input buffer
+            if seqshard:  # one captured decoder step per input buffer
                 rep, out = decoder.capture(views[0], c, n_pages)
 
                 def run():
@@ -589,13 +589,14 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
                 "kernel_us": per_call_ms * 1e3,
                 "kernel_us_source": "mean launch time over the timed region (CUDA events on the launching stream)"
-                                    + ("; the step also runs the exchange kernel" if seqshard and world > 1 else ""),
+                                    + ("; the step's kernel includes the fused exchange epilogue"
+                                       if seqshard and world > 1 else ""),
                 "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS}
     if read_gbs is not None:
         roofline.update({"read_peak_gbs": read_gbs, "frac_of_read_peak": achieved / read_gbs,
                          "read_peak_kind": "measured in this run: fs_read_bandwidth_probe over 4 GiB, best of 5"})
     api = ("flashspec_b200.fused_dequant_attention_cuda" if fused else
-           "flashspec_b200 sequence-sharded decoder (decode + exchange captured per step)" if seqshard else
+           "flashspec_b200 sequence-sharded decoder (one captured step per call)" if seqshard else
            "flashspec_b200.paged_quant_attention_cuda")
     line = {
         "metric": METRIC, "value": value, "unit": "TB/s", "n_gpus": world, "steps": args.steps,
@@ -606,7 +607,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "config": {"workload": wl.name, "global_batch": batch, "seq_len": seq_len,
                    "q_heads": wl.q_heads if not fused else 32, "kv_heads": wl.kv_heads if not fused else 32,
                    "page": 16,
-                   "parallelism": (f"sequence-shard x{world} (peer-memory exchange of O/LSE + merge)" if seqshard
+                   "parallelism": (f"sequence-shard x{world} (decode with the peer-memory exchange of O/LSE + "
+                                   "merge fused into its epilogue)" if seqshard
                                    else f"request-shard x{world}" if world > 1 else "single"),
                    "l2": ("four rotated input copies (135 MB each, > L2 together)" if fused
                           else "inputs larger than L2 (no flush)"),
@@ -620,7 +622,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                               "pinned host (side stream, double-buffered) and its output read back (second side "
                               "stream), overlapping the neighbouring steps' decode")},
         "host_us_per_call": host_us,
-        "gpu_launches": args.steps * (2 if seqshard else 1),
+        # cfg3: one fused kernel per step on N > 1 ranks; decode + merge on one
+        "gpu_launches": args.steps * (2 if seqshard and world == 1 else 1),
         "clocks": sampler.summary(t_soak, t_wall1) if sampler is not None else {},
     }
     line.update(extras)
@@ -752,18 +755,29 @@ def seqshard_sub(args, rank: int, world: int, dev, timer):
 
     wl = configs.cfg3_shard(rank, world)
     n_pages = int(wl.cache.block_table.shape[1])
-    dec = SequenceShardedDecoder()
-    replay, out = dec.capture(wl.q, wl.cache, n_pages)
-    for _ in range(max(3, args.warmup)):
-        replay()
     steps = max(20, min(args.steps, 2000))
-    ms = timer.run(lambda i: replay(), steps) / steps
-    torch.cuda.synchronize()
-    dec.close()  # raises if an exchange timed out
+
+    def timed(transport):
+        dec = SequenceShardedDecoder(transport=transport)
+        replay, out = dec.capture(wl.q, wl.cache, n_pages)
+        for _ in range(max(3, args.warmup)):
+            replay()
+        ms = timer.run(lambda i: replay(), steps) / steps
+        torch.cuda.synchronize()
+        dec.close()  # raises if an exchange timed out
+        return ms, out
+
+    ms, out = timed("p2p")
     res = {"workload": wl.name, "n_gpus": world, "us_per_call": ms * 1e3,
            "value": wl.bytes_per_call / (ms * 1e-3) / 1e12, "unit": "TB/s (whole call, all ranks)",
            "bytes_per_call": wl.bytes_per_call, "steps": steps,
-           "parallelism": f"sequence-shard x{world}, peer-memory exchange" if world > 1 else "one GPU (decode + merge)"}
+           "parallelism": (f"sequence-shard x{world}: one kernel per step, decode with the exchange fused into its "
+                           "epilogue (fs_paged_decode_exchange)" if world > 1 else "one GPU (decode + merge)"),
+           "gpu_launches_per_step": 1 if world > 1 else 2}
+    if world > 1:  # the same step as decode + separate exchange kernel, for comparison
+        ms_k, _ = timed("p2p_kernel")
+        res["two_kernel_step"] = {"us_per_call": ms_k * 1e3, "value": wl.bytes_per_call / (ms_k * 1e-3) / 1e12,
+                                  "parallelism": "decode into (O, LSE), then fs_exchange_merge"}
     if rank == 0:
         # the whole sequence on this GPU: every rank's window pool, concatenated
         pools_k, pools_v, table = [], [], torch.full_like(wl.cache.block_table, -1)

@@ -174,6 +174,9 @@ SIGNATURES = {
     "fs_exchange_close": (C.c_int, [C.c_void_p]),
     "fs_exchange_destroy": (C.c_int, [C.c_void_p]),
     "fs_exchange_merge": (C.c_int, [C.POINTER(FsExchangeArgs), C.c_void_p]),
+    "fs_paged_decode_exchange_workspace_size": (C.c_int, [C.POINTER(FsDecodeArgs), C.POINTER(C.c_size_t),
+                                                          C.POINTER(C.c_int32)]),
+    "fs_paged_decode_exchange": (C.c_int, [C.POINTER(FsDecodeArgs), C.POINTER(FsExchangeArgs), C.c_void_p]),
     "fs_page_update": (C.c_int, [C.POINTER(FsPageUpdateArgs), C.c_void_p]),
     "fs_tree_attend": (C.c_int, [C.POINTER(FsTreeArgs), C.c_void_p]),
     "fs_read_bandwidth_probe": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_int32, C.POINTER(C.c_int32),

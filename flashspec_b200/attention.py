@@ -95,23 +95,26 @@ def _i64(t: torch.Tensor) -> torch.Tensor:
     return t if t.dtype == torch.int64 and t.is_contiguous() else t.to(torch.int64).contiguous()
 
 
-def _run(entry: str, args: _lib.FsDecodeArgs, device: torch.device, splits_hint: int) -> int:
+def _run(entry: str, args: _lib.FsDecodeArgs, device: torch.device, splits_hint: int, xargs=None) -> int:
+    """Plan (cached), workspace and launch of one decode call; ``xargs`` (FsExchangeArgs)
+    selects fs_paged_decode_exchange and its own plan."""
     if torch.cuda.current_device() != device.index:
         with torch.cuda.device(device):
-            return _run(entry, args, device, splits_hint)
+            return _run(entry, args, device, splits_hint, xargs)
     lib = _lib.load()
     stream = stream_of(device)
     args.num_splits = splits_hint
     # the plan (workspace bytes, splits) depends on the shape fields and the env knobs
     key = (device.index, args.layout, args.batch, args.q_heads, args.kv_heads, args.head_dim, args.block_size,
            args.page_size, args.num_blocks, args.table_cols, args.max_seq_len, args.num_splits, args.page_begin,
-           args.page_end, bool(args.shard_o), args.q_dtype, args.kv_format,
+           args.page_end, bool(args.shard_o), args.q_dtype, args.kv_format, entry,
            tuple(os.environ.get(k) for k in _PLAN_KNOBS))
     plan = _plans.get(key)
     if plan is None:
         nbytes = C.c_size_t(0)
         splits = C.c_int32(0)
-        _lib.check(lib.fs_decode_workspace_size(C.byref(args), C.byref(nbytes), C.byref(splits)), entry)
+        size_fn = lib.fs_paged_decode_exchange_workspace_size if xargs is not None else lib.fs_decode_workspace_size
+        _lib.check(size_fn(C.byref(args), C.byref(nbytes), C.byref(splits)), entry)
         plan = _plans[key] = (nbytes.value, splits.value)
         if len(_plans) > 256:
             _plans.pop(next(iter(_plans)))
@@ -124,7 +127,10 @@ def _run(entry: str, args: _lib.FsDecodeArgs, device: torch.device, splits_hint:
         tk = _ticket_buffer(device, stream, args.batch * args.kv_heads)
         args.tickets = tk.data_ptr()
         args.ticket_count = tk.numel()
-    _lib.check(getattr(lib, entry)(C.byref(args), stream), entry)
+    if xargs is not None:
+        _lib.check(getattr(lib, entry)(C.byref(args), C.byref(xargs), stream), entry)
+    else:
+        _lib.check(getattr(lib, entry)(C.byref(args), stream), entry)
     return splits.value
 
 
@@ -209,7 +215,7 @@ def fused_dequant_attention_cuda(q: torch.Tensor, k_quant, v_quant, lengths: Opt
 def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = False, *,
                                num_splits: Optional[int] = None, page_range: Optional[Tuple[int, int]] = None,
                                partial_out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                               device_status: Optional[torch.Tensor] = None):
+                               device_status: Optional[torch.Tensor] = None, exchange=None):
     """Paged INT8 KV decode attention (backend ``cuda_paged``).
 
     ``cache`` is a PagedKVCache (this package's or the reference's): pool
@@ -221,7 +227,10 @@ def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = Fals
     Extensions used by sequence sharding: ``page_range=(lo, hi)`` restricts every
     request to logical pages [lo, hi); ``partial_out=(O fp32 [B,Hq,D], LSE fp32
     [B,Hq])`` receives the normalised partial result and its log-sum-exp instead
-    of the fp16 output (None is returned then)."""
+    of the fp16 output (None is returned then); ``exchange=(FsExchangeArgs, out)``
+    runs the window's decode with the fused exchange epilogue
+    (``fs_paged_decode_exchange``): every rank's rows are merged into ``out`` (fp16 or
+    fp32 [B, Hq, D]), which is returned."""
     _validate_query(q, "paged")
     kq, vq = cache.k_quant, cache.v_quant
     hkv = int(kq.original_shape[1])
@@ -249,7 +258,16 @@ def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = Fals
     qc = q.contiguous()
     num_pages = int(kq.values.shape[0])
     out = None
-    if partial_out is None:
+    if exchange is not None:
+        if partial_out is not None:
+            raise ValueError("exchange and partial_out are exclusive")
+        xargs, out = exchange
+        if tuple(out.shape) != tuple(qc.shape) or out.dtype not in (torch.float16, torch.float32) \
+                or not out.is_contiguous() or out.device != q.device:
+            raise ValueError("exchange output must be a contiguous fp16/fp32 [B, Hq, D] tensor on q's device")
+        xargs.out = out.data_ptr()
+        xargs.out_dtype = _lib.FS_F16 if out.dtype == torch.float16 else _lib.FS_F32
+    elif partial_out is None:
         out = torch.empty_like(qc)
     a = _decode_args(_lib.FS_LAYOUT_PAGED, qc, kq, vq, out, lengths, table, num_pages, int(cache.max_seq_len),
                      hkv, device_status, page_size=int(cache.block_size))
@@ -262,7 +280,11 @@ def paged_quant_attention_cuda(q: torch.Tensor, cache, return_stats: bool = Fals
         if tuple(o.shape) != tuple(qc.shape) or tuple(lse.shape) != tuple(qc.shape[:2]):
             raise ValueError("partial_out shapes must be [B, Hq, D] and [B, Hq]")
         a.shard_o, a.shard_lse = o.data_ptr(), lse.data_ptr()
-    splits = _run("fs_paged_decode", a, q.device, num_splits or _env_splits())
+    if exchange is not None:
+        a.out = None
+        splits = _run("fs_paged_decode_exchange", a, q.device, num_splits or _env_splits(), exchange[0])
+    else:
+        splits = _run("fs_paged_decode", a, q.device, num_splits or _env_splits())
     if not return_stats:
         return out
     dense = 2 * q.shape[0] * hkv * int(cache.max_seq_len) * d * qc.element_size()

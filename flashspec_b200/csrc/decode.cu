@@ -40,6 +40,7 @@
 #include "common.h"
 #include "generic.h"
 #include "ptx.cuh"
+#include "xwords.cuh"
 
 namespace fsb {
 
@@ -78,6 +79,13 @@ struct DecodeParams {
   int piece_cost;       // balanced kernel: virtual pages charged per (request, kv head) pair
   int debug_mode;       // profiling only (FLASHSPEC_DEBUG_MODE)
   int sym;              // FS_KV_SYMMETRIC: per-token scales [blocks, 16], no zero points
+  // fused exchange epilogue (fs_paged_decode_exchange); xworld == 0 otherwise
+  void* xbufs[kXMaxRanks];
+  void* xout;
+  uint32_t* xstatus;
+  int64_t xslot;
+  int64_t xtimeout_ns;
+  int xworld, xrank, xout_dtype;
 };
 
 // Shared-memory plan of one CTA: a ring of kNS page stages (K 2 KB + V 2 KB, 1024-byte
@@ -441,6 +449,88 @@ __device__ __forceinline__ void write_final(const DecodeParams& p, size_t row, i
   }
 }
 
+// Fused exchange epilogue of a sequence-sharded step: this rank's normalised (O, LSE)
+// rows of pair (b, h) -- staged in shared memory as xo [G][128], xl [G] -- go as tagged
+// words (xwords.cuh) into slot `xrank` of every rank's exchange buffer; then the CTA
+// merges every rank's rows of the pair with the log-sum-exp rule (the combine of
+// triton_fused.py:446-503 on one partial per rank) as they arrive, and writes them to
+// xout.  Waits end at xtimeout_ns: the CTA then sets FS_DEV_TIMEOUT and writes NaN.
+// The pair's call counter in this rank's buffer gives the epoch (tag and parity).
+__device__ __forceinline__ void exchange_pair(const DecodeParams& p, int b, int h, int bh, const float* xo,
+                                           const float* xl, int tid, int nthreads) {
+  uint8_t* own = static_cast<uint8_t*>(p.xbufs[p.xrank]);
+  uint32_t* calls = reinterpret_cast<uint32_t*>(own + kXPairCountersOffset);
+  const uint32_t e = calls[bh] + 1u;  // written by this pair's previous call on this GPU
+  const size_t poff = exchange_parity_offset(e, p.xslot);
+  const int64_t rows = (int64_t)p.B * p.Hq;
+  const int64_t row0 = (int64_t)b * p.Hq + (int64_t)h * p.G;
+  const int n = p.G * kD;
+  for (int r = 0; r < p.xworld; ++r) {
+    if (r == p.xrank) continue;  // this rank's rows are merged from shared memory
+    uint64_t* dst = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(p.xbufs[r]) + poff) + (size_t)p.xrank * p.xslot;
+    for (int i = tid; i < n; i += nthreads) st_word(dst + row0 * kD + i, xo[i], e);
+    if (tid < p.G) st_word(dst + rows * kD + row0 + tid, xl[tid], e);
+  }
+  const uint64_t* data = reinterpret_cast<const uint64_t*>(own + poff);
+  const uint64_t deadline = globaltimer_ns() + (uint64_t)p.xtimeout_ns;
+  bool ok = true;
+  for (int i = tid; i < n; i += nthreads) {
+    const int qg = i >> 7;
+    float lse[kXMaxRanks], o[kXMaxRanks];
+    uint64_t wl[kXMaxRanks], wo[kXMaxRanks];
+    // first look: every rank's two words at once (independent loads in flight)
+#pragma unroll
+    for (int r = 0; r < kXMaxRanks; ++r)
+      if (r < p.xworld && r != p.xrank) {
+        wl[r] = ld_word(data + (size_t)r * p.xslot + rows * kD + row0 + qg);
+        wo[r] = ld_word(data + (size_t)r * p.xslot + row0 * kD + i);
+      }
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kXMaxRanks; ++r) {
+      lse[r] = -INFINITY;
+      o[r] = 0.f;
+      if (r >= p.xworld) continue;
+      if (r == p.xrank) {
+        lse[r] = xl[qg];
+        o[r] = xo[i];
+      } else if (ok) {
+        const uint64_t* pl = data + (size_t)r * p.xslot + rows * kD + row0 + qg;
+        const uint64_t* po = data + (size_t)r * p.xslot + row0 * kD + i;
+        if ((uint32_t)(wl[r] >> 32) == e)
+          lse[r] = __uint_as_float((uint32_t)wl[r]);
+        else
+          ok = wait_word(pl, e, deadline, lse[r]);
+        if (ok) {
+          if ((uint32_t)(wo[r] >> 32) == e)
+            o[r] = __uint_as_float((uint32_t)wo[r]);
+          else
+            ok = wait_word(po, e, deadline, o[r]);
+        }
+      }
+      M = fmaxf(M, lse[r]);
+    }
+    float W = 0.f, O = 0.f;
+    if (ok && M != -INFINITY)
+#pragma unroll
+      for (int r = 0; r < kXMaxRanks; ++r)
+        if (r < p.xworld) {
+          const float w = lse[r] == -INFINITY ? 0.f : expf(lse[r] - M);
+          W += w;
+          O += w * o[r];
+        }
+    const float v = !ok ? __int_as_float(0x7fc00000) : W > 0.f ? O / W : 0.f;
+    const size_t at = (size_t)row0 * kD + i;
+    if (p.xout_dtype == FS_F16)
+      static_cast<__half*>(p.xout)[at] = __float2half_rn(v);
+    else
+      static_cast<float*>(p.xout)[at] = v;
+  }
+  if (!ok && p.xstatus != nullptr) atomicOr(p.xstatus, FS_DEV_TIMEOUT);
+  __syncthreads();  // every thread has read this call's words before the epoch advances
+  if (tid == 0) calls[bh] = e;
+}
+
 // ==================================================================================
 // Split kernel: one CTA = one (request, kv head, split).  Warps 0..kW-1 consume pages;
 // warp kW is the producer that keeps the ring full with TMA tile loads and cp.async
@@ -593,6 +683,12 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   constexpr int kThreads = (kW + 1) * 32;
   const int nout = p.G * kD;
   const float kLn2 = 0.6931471805599453f;
+  // fused exchange: the pair's merged rows are staged at the end of the ring region
+  constexpr int kXStage = (L::kStageRegion - (kMaxG * kD + kMaxG) * 4) & ~15;
+  static_assert(kXStage >= (2 + kD) * kW * kMaxG * 4, "exchange staging overlaps the warp merge");
+  const bool xmode = p.xworld > 0;
+  float* xo = reinterpret_cast<float*>(base_p + kXStage);
+  float* xl = xo + kMaxG * kD;
   for (int idx = tid; idx < nout; idx += kThreads) {
     const int qg = idx >> 7;
     const int d = idx & (kD - 1);
@@ -609,7 +705,10 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     const float o = Lsum > 0.f ? O / Lsum : 0.f;
     const float lse = Lsum > 0.f ? (M + log2f(Lsum)) * kLn2 : -INFINITY;
     const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
-    if (S == 1) {
+    if (S == 1 && xmode) {
+      xo[idx] = o;
+      if (d == 0) xl[qg] = lse;
+    } else if (S == 1) {
       write_final(p, row, d, o, lse);
     } else {
       const size_t prow = ((size_t)bh * S + split) * p.G + qg;
@@ -617,7 +716,13 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       if (d == 0) p.part_lse[prow] = lse;
     }
   }
-  if (S == 1) return;
+  if (S == 1) {
+    if (xmode) {
+      __syncthreads();
+      exchange_pair(p, b, h, bh, xo, xl, tid, kThreads);
+    }
+    return;
+  }
 
   // ---- split-K: the last CTA of this (request, kv head) merges -------------------
   __shared__ int s_last;
@@ -634,7 +739,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   // free now): w[s][q] = exp(lse_s - M) / sum_s exp(lse_s - M); empty partials weigh 0
   float* wsm = reinterpret_cast<float*>(base_p);  // [S][G] (+ [G] merged LSE)
   const int nw = S * p.G;
-  const bool fits = (nw + p.G) * 4 <= L::kStageRegion;
+  const bool fits = (nw + p.G) * 4 <= kXStage;
   if (fits) {
     const size_t prow0 = (size_t)bh * S * p.G;
     for (int k = tid; k < nw; k += kThreads) wsm[k] = __ldcg(p.part_lse + prow0 + k);
@@ -683,10 +788,15 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       }
       const float lse_out = wsm[nw + qg];
       const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
-      write_final(p, row, d, o.x, lse_out);
-      write_final(p, row, d + 1, o.y, lse_out);
-      write_final(p, row, d + 2, o.z, lse_out);
-      write_final(p, row, d + 3, o.w, lse_out);
+      if (xmode) {
+        *reinterpret_cast<float4*>(xo + 4 * u4) = o;
+        if (d == 0) xl[qg] = lse_out;
+      } else {
+        write_final(p, row, d, o.x, lse_out);
+        write_final(p, row, d + 1, o.y, lse_out);
+        write_final(p, row, d + 2, o.z, lse_out);
+        write_final(p, row, d + 3, o.w, lse_out);
+      }
     }
   }
   for (int idx = fits ? nout : tid; idx < nout; idx += kThreads) {
@@ -710,9 +820,18 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       o = W > 0.f ? O / W : 0.f;
       lse_out = W > 0.f ? M + logf(W) : -INFINITY;
     }
-    write_final(p, (size_t)b * p.Hq + (size_t)h * p.G + qg, d, o, lse_out);
+    if (xmode) {
+      xo[idx] = o;
+      if (d == 0) xl[qg] = lse_out;
+    } else {
+      write_final(p, (size_t)b * p.Hq + (size_t)h * p.G + qg, d, o, lse_out);
+    }
   }
   if (tid == 0) p.counters[bh] = 0u;  // leave the ticket clean for the next call
+  if (xmode) {
+    __syncthreads();
+    exchange_pair(p, b, h, bh, xo, xl, tid, kThreads);
+  }
 }
 
 // ==================================================================================
@@ -1563,16 +1682,59 @@ static int validate(const FsDecodeArgs* a, int layout) {
   return FS_OK;
 }
 
+// Plan of a decode with the fused exchange epilogue: the split kernel, one wave at most
+// (every CTA resident at once, so a CTA waiting for its peers never holds a slot that
+// another CTA of the same call needs); FS_ERR_UNSUPPORTED when the pairs alone exceed
+// one wave or the exchange's per-pair counters.
+static int exchange_plan(const FsDecodeArgs* a, int device, int forced, Plan* pl) {
+  const int shape = forced >= 0 ? forced : kDefaultShape;
+  const int64_t pairs = (int64_t)a->batch * a->kv_heads;
+  const int64_t slots = resident_ctas(device, shape);
+  if (pairs > slots || pairs > kXMaxPairs) return FS_ERR_UNSUPPORTED;
+  int64_t s = resolve_splits(a, device, shape);
+  if (s * pairs > slots) s = slots / pairs;
+  *pl = Plan{false, (int)std::max<int64_t>(s, 1), 0, shape};
+  return FS_OK;
+}
+
+static int validate_exchange(const FsDecodeArgs* a, const FsExchangeArgs* x) {
+  if (x == nullptr || x->world < 1 || x->world > kXMaxRanks || x->rank < 0 || x->rank >= x->world ||
+      x->out == nullptr || x->timeout_ns <= 0)
+    return FS_ERR_INVALID_ARGUMENT;
+  if (x->out_dtype != FS_F16 && x->out_dtype != FS_F32) return FS_ERR_UNSUPPORTED;
+  if (a->shard_o != nullptr || a->shard_lse != nullptr) return FS_ERR_INVALID_ARGUMENT;
+  const int64_t rows = (int64_t)a->batch * a->q_heads;
+  if (x->slot_floats < rows * (a->head_dim + 1) || x->slot_floats % 64) return FS_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < x->world; ++r)
+    if (x->bufs[r] == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  if (!exchange_buffers_match(x)) return FS_ERR_INVALID_ARGUMENT;
+  if (!tuned_shape(a)) return FS_ERR_UNSUPPORTED;
+  return FS_OK;
+}
+
 template <bool kPaged>
-static int launch_decode(const FsDecodeArgs* a, void* stream) {
+static int launch_decode(const FsDecodeArgs* a_in, void* stream, const FsExchangeArgs* x = nullptr) {
+  FsDecodeArgs ax;
+  const FsDecodeArgs* a = a_in;
+  if (x != nullptr && a_in != nullptr) {  // the exchange writes x->out; the decode's own output is unused
+    ax = *a_in;
+    ax.out = x->out;
+    a = &ax;
+  }
   int st = validate(a, kPaged ? FS_LAYOUT_PAGED : FS_LAYOUT_CONTIGUOUS);
   if (st != FS_OK) return st;
+  if (x != nullptr && (st = validate_exchange(a_in, x)) != FS_OK) return st;
   int device = 0;
   if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
   if (!tuned_shape(a)) return launch_generic_decode(a, device, stream);
   const int forced = shape_choice();
   if ((st = configure_shapes<kPaged>(device, forced)) != FS_OK) return st;
-  const Plan pl = make_plan(a, device, forced);
+  Plan pl;
+  if (x != nullptr) {
+    if ((st = exchange_plan(a, device, forced, &pl)) != FS_OK) return st;
+  } else {
+    pl = make_plan(a, device, forced);
+  }
   const int shape = pl.shape;
   const size_t need = pl.balanced ? workspace_balanced(a, pl.ctas, shape) : workspace_for(a, pl.splits);
   if (need > 0 && (a->workspace == nullptr || a->workspace_bytes < need)) return FS_ERR_WORKSPACE;
@@ -1615,6 +1777,16 @@ static int launch_decode(const FsDecodeArgs* a, void* stream) {
   p.piece_cost = piece_cost();
   p.debug_mode = debug_mode();
   p.sym = a->kv_format == FS_KV_SYMMETRIC;
+  if (x != nullptr) {
+    for (int r = 0; r < x->world; ++r) p.xbufs[r] = x->bufs[r];
+    p.xout = x->out;
+    p.xstatus = x->device_status;
+    p.xslot = x->slot_floats;
+    p.xtimeout_ns = x->timeout_ns;
+    p.xworld = x->world;
+    p.xrank = x->rank;
+    p.xout_dtype = x->out_dtype;
+  }
   if (need > 0) {
     const size_t G = (size_t)p.G;
     const size_t units = pl.balanced ? (size_t)pl.ctas * kShapes[shape].warps * 2 * G
@@ -1659,6 +1831,26 @@ int fs_decode_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* spli
   *bytes = pl.balanced ? fsb::workspace_balanced(a, pl.ctas, pl.shape) : fsb::workspace_for(a, pl.splits);
   if (splits_out) *splits_out = pl.balanced ? 0 : pl.splits;
   return FS_OK;
+}
+
+int fs_paged_decode_exchange_workspace_size(const FsDecodeArgs* a, size_t* bytes, int32_t* splits_out) {
+  if (a == nullptr || bytes == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  if (a->layout != FS_LAYOUT_PAGED || !fsb::tuned_shape(a)) return FS_ERR_UNSUPPORTED;
+  int device = 0;
+  if (cudaError_t e = cudaGetDevice(&device); e != cudaSuccess) return fsb::fail_cuda("cudaGetDevice", e);
+  const int forced = fsb::shape_choice();
+  int st = fsb::configure_shapes<true>(device, forced);
+  if (st != FS_OK) return st;
+  fsb::Plan pl;
+  if ((st = fsb::exchange_plan(a, device, forced, &pl)) != FS_OK) return st;
+  *bytes = fsb::workspace_for(a, pl.splits);
+  if (splits_out) *splits_out = pl.splits;
+  return FS_OK;
+}
+
+int fs_paged_decode_exchange(const FsDecodeArgs* args, const FsExchangeArgs* x, void* stream) {
+  if (x == nullptr) return FS_ERR_INVALID_ARGUMENT;
+  return fsb::launch_decode<true>(args, stream, x);
 }
 
 int fs_fused_decode(const FsDecodeArgs* args, void* stream) { return fsb::launch_decode<false>(args, stream); }

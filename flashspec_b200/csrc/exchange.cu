@@ -10,16 +10,10 @@
 // and merges the slice locally as every rank's words for it arrive, waiting at most
 // timeout_ns.
 //
-// Protocol: every value travels as one naturally aligned 8-byte word, (value bits,
-// call epoch) -- single-copy atomic -- so a receiver knows a word has arrived when its
-// tag equals the current epoch, without fences or separate flags.  Buffer layout
-// (bytes): [0, 256) per-CTA call counters (epoch of CTA c's last completed call);
-// [256, 264) the slot size the buffer was created with (read back by fs_exchange_open,
-// so fs_exchange_merge can refuse a slot size that would store past a peer's buffer);
-// from 512 two epoch parities x kXMaxRanks slots of slot_floats words (O [rows][D],
-// then LSE [rows]).  Parity: a peer may begin its next call as soon as it has this rank's words,
-// so its next words land in the other parity while this rank still reads the current
-// one; it cannot get two calls ahead, as that needs this rank's words of the next call.
+// Protocol and buffer layout: xwords.cuh.  Parity: a peer may begin its next call as
+// soon as it has this rank's words, so its next words land in the other parity while
+// this rank still reads the current one; it cannot get two calls ahead, as that needs
+// this rank's words of the next call.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -31,16 +25,11 @@
 #include "../../include/flashspec_b200.h"
 #include "common.h"
 #include "ptx.cuh"
+#include "xwords.cuh"
 
 namespace fsb {
 
-constexpr int kXMaxRanks = FS_EXCHANGE_MAX_RANKS;
-constexpr int kXMaxCtas = 64;
 constexpr int kXThreads = 256;
-constexpr size_t kXCountersBytes = 256;  // kXMaxCtas 32-bit call counters
-constexpr size_t kXSlotSizeOffset = kXCountersBytes;  // int64 slot_floats of the buffer
-constexpr size_t kXDataOffset = 512;
-static_assert(kXMaxCtas * 4 <= kXCountersBytes, "call counters");
 
 // Slot size of every exchange buffer this process created or mapped, by address.
 static std::mutex g_xbuf_mu;
@@ -56,37 +45,13 @@ static void forget_buffer(const void* p) {
   g_xbuf_slots.erase(p);
 }
 
-// true when every buffer of the call is known here and was made for this slot size
-static bool buffers_match(const FsExchangeArgs* a) {
+bool exchange_buffers_match(const FsExchangeArgs* a) {
   std::lock_guard<std::mutex> lock(g_xbuf_mu);
   for (int p = 0; p < a->world; ++p) {
     const auto it = g_xbuf_slots.find(a->bufs[p]);
     if (it == g_xbuf_slots.end() || it->second != a->slot_floats) return false;
   }
   return true;
-}
-
-__device__ __forceinline__ void st_word(uint64_t* p, float v, uint32_t tag) {
-  const uint64_t w = ((uint64_t)tag << 32) | __float_as_uint(v);
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-
-__device__ __forceinline__ uint64_t ld_word(const uint64_t* p) {
-  uint64_t w;
-  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-  return w;
-}
-
-// Value of the word at p once it carries tag e; false when the deadline passes first.
-__device__ __forceinline__ bool wait_word(const uint64_t* p, uint32_t e, uint64_t deadline, float& v) {
-  for (unsigned n = 0;; ++n) {
-    const uint64_t w = ld_word(p);
-    if ((uint32_t)(w >> 32) == e) {
-      v = __uint_as_float((uint32_t)w);
-      return true;
-    }
-    if ((n & 255u) == 255u && globaltimer_ns() > deadline) return false;
-  }
 }
 
 __global__ void __launch_bounds__(kXThreads) exchange_merge_kernel(const FsExchangeArgs a, int rows_per_cta) {
@@ -97,7 +62,7 @@ __global__ void __launch_bounds__(kXThreads) exchange_merge_kernel(const FsExcha
   uint8_t* own = static_cast<uint8_t*>(a.bufs[a.rank]);
   uint32_t* calls = reinterpret_cast<uint32_t*>(own);
   const uint32_t e = calls[c] + 1u;  // written by this CTA's previous call on this GPU
-  const size_t parity_off = kXDataOffset + (size_t)(e & 1u) * kXMaxRanks * a.slot_floats * 8;
+  const size_t parity_off = exchange_parity_offset(e, a.slot_floats);
   const int64_t lse_at = a.rows * D;
   const uint64_t deadline = globaltimer_ns() + (uint64_t)a.timeout_ns;
 
@@ -225,7 +190,7 @@ int fs_exchange_merge(const FsExchangeArgs* a, void* stream) {
     if (a->bufs[p] == nullptr) return FS_ERR_INVALID_ARGUMENT;
   // every buffer must come from fs_exchange_create / fs_exchange_open with this slot size:
   // a larger one would make the kernel store past the end of a peer's buffer
-  if (!buffers_match(a)) return FS_ERR_INVALID_ARGUMENT;
+  if (!exchange_buffers_match(a)) return FS_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(a->o_mine) & 15) return FS_ERR_ALIGNMENT;
   // slices of whole rows whose O part is a multiple of 4 floats
   int rows_per_cta = (int)((a->rows + kXMaxCtas - 1) / kXMaxCtas);

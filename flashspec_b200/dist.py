@@ -6,12 +6,14 @@ Two strategies (the reference has no multi-GPU path):
   and runs the single-GPU kernel on them.  No communication; see ``request_shard``.
 * sequence sharding of long requests (config 3): rank r owns the contiguous logical
   pages ``page_window(n_pages, r, N)`` of every request and only those pages are
-  resident on it.  Each rank computes a normalised partial (O fp32, LSE fp32) over
-  its window with the page-window mode of the decode kernel; one exchange kernel
-  (``fs_exchange_merge``) stores the rank's rows into every rank's exchange buffer over
-  NVLink and merges all ranks' rows with the log-sum-exp rule -- the same math as the
-  split-K combine (src/flashspec/triton_fused.py:446-503) applied across GPUs.  The
-  NCCL all-gather + ``fs_merge_partials`` step remains as ``transport="nccl"``.
+  resident on it.  By default one kernel per step (``fs_paged_decode_exchange``): the
+  decode of the rank's window whose epilogue -- the CTA that finishes a (request, kv
+  head) pair -- stores the pair's normalised (O, LSE) rows into every rank's exchange
+  buffer over NVLink and merges all ranks' rows with the log-sum-exp rule, the same
+  math as the split-K combine (src/flashspec/triton_fused.py:446-503) applied across
+  GPUs.  ``transport="p2p_kernel"`` runs the decode into (O, LSE) and a separate
+  exchange kernel (``fs_exchange_merge``); ``transport="nccl"`` an all-gather +
+  ``fs_merge_partials``.
 """
 
 from __future__ import annotations
@@ -121,6 +123,14 @@ class PeerExchange:
         _lib.check(self._lib.fs_exchange_merge(C.byref(a), stream_of(self.device)), "fs_exchange_merge")
         return out
 
+    def decode(self, q: torch.Tensor, cache, window: Tuple[int, int], out: torch.Tensor) -> torch.Tensor:
+        """The whole step in one kernel (``fs_paged_decode_exchange``): decode of this
+        rank's page window whose epilogue stores the rows to every rank and merges them
+        into ``out``.  A set of buffers serves either this or ``merge``, not both."""
+        from .attention import paged_quant_attention_cuda
+
+        return paged_quant_attention_cuda(q, cache, page_range=window, exchange=(self._args, out))
+
     def check(self) -> None:
         """Raise if any merge so far gave up waiting for a peer (FS_DEV_TIMEOUT in the
         status word).  Waits for this device's queued work.  A timed-out call wrote NaN
@@ -156,13 +166,15 @@ class PeerExchange:
 class SequenceShardedDecoder:
     """Decode one batch whose KV pages are split across the ranks of ``group``.
 
-    Default (CUDA) path per call: the decode kernel writes the rank's partial (O, LSE)
-    into a preallocated [O | LSE] fp32 buffer; with more than one rank the peer-memory
-    exchange (``PeerExchange``, transport "p2p") delivers every rank's rows to every rank
-    and merges them into the fp16 output in one kernel, or (transport "nccl", also
+    Default (CUDA) path per call, with more than one rank: transport "p2p" runs the
+    decode of the rank's window with the fused exchange epilogue (one kernel; shapes it
+    does not take fall back to "p2p_kernel"); "p2p_kernel" writes the rank's partial
+    (O, LSE) into a preallocated [O | LSE] fp32 buffer and the peer-memory exchange
+    (``PeerExchange.merge``) delivers every rank's rows to every rank and merges them
+    into the fp16 output; or (transport "nccl", also
     ``FLASHSPEC_EXCHANGE=nccl``) an out-of-place ``all_gather_into_tensor`` collects the
     slots and ``fs_merge_partials`` merges them.  ``capture`` records the whole step as a
-    CUDA graph (single-rank groups, or any group on the p2p transport).
+    CUDA graph (single-rank groups, or any group on the p2p transports).
 
     ``partial_fn(q, cache, (lo, hi)) -> (O, LSE)`` and ``merge_fn(O[N], LSE[N], dtype)``
     replace the CUDA steps (then the generic list all-gather is used); tests run the
@@ -178,13 +190,15 @@ class SequenceShardedDecoder:
         self._calls = 0
         self.partial_fn = partial_fn
         self.merge_fn = merge_fn
-        # multi-rank CUDA steps: "p2p" (peer-memory exchange kernel) or "nccl" (all-gather)
+        # multi-rank CUDA steps: "p2p" (decode with the fused exchange epilogue),
+        # "p2p_kernel" (decode, then the exchange kernel) or "nccl" (all-gather)
         self.transport = transport or os.environ.get("FLASHSPEC_EXCHANGE", "p2p")
-        if self.transport not in ("p2p", "nccl"):
-            raise ValueError("transport must be 'p2p' or 'nccl'")
+        if self.transport not in ("p2p", "p2p_kernel", "nccl"):
+            raise ValueError("transport must be 'p2p', 'p2p_kernel' or 'nccl'")
         self.timeout_ns = int(timeout_ms * 1e6)
         self._bufs = {}
         self._xch = {}
+        self._unfusable = set()
 
     @property
     def world(self) -> int:
@@ -230,17 +244,29 @@ class SequenceShardedDecoder:
         mine, gather = bufs
         o = mine[: rows * d].view(b, hq, d)
         lse = mine[rows * d: rows * d + rows].view(b, hq)
-        paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages), partial_out=(o, lse))
-        if self.world > 1 and self.transport == "p2p":
-            xkey = (q.device, slot)
-            xch = self._xch.get(xkey)
-            if xch is None:
-                xch = self._xch[xkey] = PeerExchange(self.group, q.device, slot, self.timeout_ns)
-            out = xch.merge(o, lse, torch.empty(q.shape, dtype=out_dtype, device=q.device))
+        if self.world > 1 and self.transport in ("p2p", "p2p_kernel"):
+            # "p2p": one kernel per step (decode + exchange epilogue) where the shape
+            # allows it; otherwise, and with "p2p_kernel", decode then exchange kernel
+            fused = self.transport == "p2p" and (q.device, b, hq, d, n_pages) not in self._unfusable
+            out = torch.empty(q.shape, dtype=out_dtype, device=q.device)
+            if fused:
+                xch = self._exchange(q.device, slot, "fused")
+                try:
+                    xch.decode(q, cache, self.window(n_pages), out)
+                except ValueError as e:
+                    if "(status 2)" not in str(e):  # FS_ERR_UNSUPPORTED: shape outside the fused kernel
+                        raise
+                    self._unfusable.add((q.device, b, hq, d, n_pages))
+                    fused = False
+            if not fused:
+                paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages), partial_out=(o, lse))
+                xch = self._exchange(q.device, slot, "kernel")
+                xch.merge(o, lse, out)
             self._calls += 1
             if self.check_every > 0 and self._calls % self.check_every == 0:
                 xch.check()
             return out
+        paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages), partial_out=(o, lse))
         if self.world > 1:  # out of place: the send buffer is not a view of the receive buffer
             dist.all_gather_into_tensor(gather.view(-1), mine, group=self.group)
         else:
@@ -251,6 +277,15 @@ class SequenceShardedDecoder:
         _lib.check(_lib.load().fs_merge_partials(base, base + 4 * rows * d, self.world, rows, d, slot, out.data_ptr(),
                                                  code, stream_of(q.device)), "fs_merge_partials")
         return out
+
+    def _exchange(self, device, slot: int, mode: str) -> "PeerExchange":
+        """The group's exchange buffers for one slot size and mode (created collectively
+        on first use: every rank reaches it in the same call)."""
+        key = (device, slot, mode)
+        xch = self._xch.get(key)
+        if xch is None:
+            xch = self._xch[key] = PeerExchange(self.group, device, slot, self.timeout_ns)
+        return xch
 
     def check(self) -> None:
         """Raise RuntimeError if an exchange of this decoder has timed out (see
@@ -290,8 +325,8 @@ class SequenceShardedDecoder:
         the step on the current contents of q / cache and refreshes ``out``.  Multi-rank
         steps are captured only with the peer-memory exchange (the NCCL step runs eagerly);
         every rank must then replay its graph the same number of times."""
-        if self.world > 1 and self.transport != "p2p":
-            raise ValueError("capture() of a multi-rank step needs transport='p2p'; NCCL steps run eagerly")
+        if self.world > 1 and self.transport == "nccl":
+            raise ValueError("capture() of a multi-rank step needs a p2p transport; NCCL steps run eagerly")
         side = torch.cuda.Stream(device=q.device)
         side.wait_stream(torch.cuda.current_stream(q.device))
         with torch.cuda.stream(side):

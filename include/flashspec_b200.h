@@ -196,6 +196,25 @@ int fs_exchange_close(void* peer_buf);
 int fs_exchange_destroy(void* buf);
 int fs_exchange_merge(const FsExchangeArgs* args, void* stream);
 
+/* Sequence-sharded decode step in ONE kernel: the paged decode of this rank's page
+ * window (args->page_begin / page_end) whose epilogue is the exchange -- the CTA that
+ * finishes a (request, kv head) pair stores the pair's normalised (O, LSE) rows straight
+ * into every rank's exchange buffer and merges every rank's rows of the pair into
+ * x->out [batch, q_heads, head_dim] (FS_F16 or FS_F32), with no partial round trip
+ * through this GPU's memory and no second launch.  Same buffers, waits, timeout and
+ * status word as fs_exchange_merge (x->o_mine, lse_mine, rows, head_dim are ignored);
+ * args->out and shard_o / shard_lse must be NULL.  Tuned shapes only (head_dim 128,
+ * pages = quant blocks = 16 tokens, fp16 q) and at most one wave of CTAs per call
+ * (batch * kv_heads <= resident CTAs, <= 4096 pairs), else FS_ERR_UNSUPPORTED.  The
+ * split-K workspace and tickets are those fs_paged_decode_exchange_workspace_size names.
+ * A set of exchange buffers serves either this entry point or fs_exchange_merge, not
+ * both.  Replaces the same step as fs_exchange_merge: the reference has no multi-GPU
+ * path; per GPU it is paged_quant_attention_triton (src/flashspec/triton_paged.py:453)
+ * over a page range, and the merge is _combine_splits_kernel
+ * (src/flashspec/triton_fused.py:446-503) across ranks. */
+int fs_paged_decode_exchange_workspace_size(const FsDecodeArgs* args, size_t* workspace_bytes, int32_t* splits);
+int fs_paged_decode_exchange(const FsDecodeArgs* args, const FsExchangeArgs* x, void* stream);
+
 /* Affine INT8 quantization of x [n_lead, seq_len, head_dim] (dtype x_dtype,
  * contiguous) in blocks of block_size tokens, zero-padding the last block:
  * values [n_lead, nblk, block_size, head_dim], scale/zero_point [n_lead, nblk].

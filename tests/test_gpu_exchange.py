@@ -121,6 +121,82 @@ def test_missing_peer_times_out_and_reports():
         lib.fs_exchange_destroy(silent_peer)
 
 
+def _fused_call(lib, wl, bufs, rank, slot, out, status, timeout_ns, num_splits):
+    """fs_paged_decode_exchange through the C ABI: the whole window (every page) of wl."""
+    import flashspec_b200 as fs
+    from flashspec_b200 import _lib
+
+    x = _lib.FsExchangeArgs()
+    x.world, x.rank = len(bufs), rank
+    for r, b in enumerate(bufs):
+        x.bufs[r] = b
+    x.slot_floats, x.timeout_ns, x.device_status = slot, timeout_ns, status.data_ptr()
+    fs.paged_quant_attention_cuda(wl.q, wl.cache, num_splits=num_splits, exchange=(x, out))
+
+
+@pytest.mark.parametrize("num_splits", [1, 3])
+def test_fused_one_rank_exchange_equals_paged_decode(num_splits):
+    """With one rank the fused decode + exchange epilogue merges a single partial with
+    weight 1, so its fp16 output must equal fs_paged_decode's bit for bit (same splits),
+    call after call as the per-pair epoch advances; fp32 output must round to it."""
+    _need_gpu()
+    import flashspec_b200 as fs
+    from flashspec_b200 import _lib
+
+    lib = _lib.load()
+    wl, o, lse = _partial()
+    rows, d = lse.numel(), o.shape[-1]
+    slot = (rows * (d + 1) + 63) // 64 * 64
+    ref = fs.paged_quant_attention_cuda(wl.q, wl.cache, num_splits=num_splits)
+    buf = _create(lib, slot)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        for _ in range(3):
+            out = torch.full_like(wl.q, float("nan"))
+            _fused_call(lib, wl, [buf], 0, slot, out, status, 10**9, num_splits)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            assert torch.equal(out, ref)
+        out32 = torch.full(wl.q.shape, float("nan"), dtype=torch.float32, device="cuda")
+        _fused_call(lib, wl, [buf], 0, slot, out32, status, 10**9, num_splits)
+        torch.cuda.synchronize()
+        assert torch.equal(out32.half(), ref)
+    finally:
+        torch.cuda.synchronize()
+        lib.fs_exchange_destroy(buf)
+
+
+def test_fused_missing_peer_times_out_and_reports():
+    """Rank 0 of a two-rank fused step whose rank 1 never runs: each pair's epilogue
+    waits for the peer's tagged words, which nothing writes, gives up after 20 ms, sets
+    FS_DEV_TIMEOUT and writes NaN; again on a second call; the device stays usable, and
+    buffers of another slot size are refused before launch."""
+    _need_gpu()
+    from flashspec_b200 import _lib
+
+    lib = _lib.load()
+    wl, o, lse = _partial()
+    rows, d = lse.numel(), o.shape[-1]
+    slot = (rows * (d + 1) + 63) // 64 * 64
+    mine, silent_peer = _create(lib, slot), _create(lib, slot)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    try:
+        for _ in range(2):
+            status.zero_()
+            out = torch.zeros_like(wl.q)
+            _fused_call(lib, wl, [mine, silent_peer], 0, slot, out, status, 20 * 10**6, 2)
+            torch.cuda.synchronize()
+            assert int(status.item()) & _lib.FS_DEV_TIMEOUT
+            assert bool(torch.isnan(out).all()), "a timed-out step must not return values"
+        assert float(torch.ones(4, device="cuda").sum()) == 4.0
+        with pytest.raises(ValueError, match="status 1"):
+            _fused_call(lib, wl, [mine, silent_peer], 0, slot + 64, torch.zeros_like(wl.q), status, 20 * 10**6, 2)
+    finally:
+        torch.cuda.synchronize()
+        lib.fs_exchange_destroy(mine)
+        lib.fs_exchange_destroy(silent_peer)
+
+
 def test_decoder_check_raises_after_a_timeout():
     """PeerExchange.check() turns FS_DEV_TIMEOUT into an exception on the host."""
     _need_gpu()
@@ -142,7 +218,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, transport):
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
 
@@ -165,7 +241,7 @@ def _rank_main(rank, world, port, out_dir):
     oc = O.OPagedCache(oq(wl.cache.k_quant), oq(wl.cache.v_quant), wl.cache.block_table.cpu().numpy(),
                        wl.cache.lengths.cpu().numpy(), 16, int(wl.cache.max_seq_len))
     full = torch.from_numpy(O.paged_quant_attention(wl.q.cpu().numpy(), oc).astype("float32")).to(wl.q.device)
-    dec = SequenceShardedDecoder(transport="p2p")
+    dec = SequenceShardedDecoder(transport=transport)
     errs = []
     for _ in range(3):
         out = dec(wl.q, wl.cache, n_pages)
@@ -177,19 +253,25 @@ def _rank_main(rank, world, port, out_dir):
         errs.append(float(((gout.float() - full.float()).abs() - RTOL * full.float().abs()).max()))
     torch.cuda.synchronize()
     status = [int(x.status.item()) for x in dec._xch.values()]
+    modes = sorted({k[2] for k in dec._xch})
+    assert modes == (["fused"] if transport == "p2p" else ["kernel"]), modes
     (Path(out_dir) / f"rank{rank}.txt").write_text(f"{max(errs)} {max(status)}")
     dec.close()
     dist.destroy_process_group()
 
 
-def test_two_ranks_match_single_gpu_decode():
+@pytest.mark.parametrize("transport", ["p2p", "p2p_kernel"])
+def test_two_ranks_match_the_oracle(transport):
+    """Two ranks (one GPU each) decode their page windows and exchange; rank r's merged
+    output must match the CPU oracle on the whole sequence, eagerly and replayed from a
+    CUDA graph, with the fused epilogue ("p2p") and with the separate exchange kernel."""
     _need_gpu(2)
     import torch.multiprocessing as mp
 
     port = _free_port()
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
-        procs = [ctx.Process(target=_rank_main, args=(r, 2, port, d)) for r in range(2)]
+        procs = [ctx.Process(target=_rank_main, args=(r, 2, port, d, transport)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
