@@ -622,8 +622,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                               "pinned host (side stream, double-buffered) and its output read back (second side "
                               "stream), overlapping the neighbouring steps' decode")},
         "host_us_per_call": host_us,
-        # cfg3: one fused kernel per step on N > 1 ranks; decode + merge on one
-        "gpu_launches": args.steps * (2 if seqshard and world == 1 else 1),
+        "gpu_launches": args.steps,  # cfg3: one kernel per step (fused exchange on N > 1, plain decode on 1)
         "clocks": sampler.summary(t_soak, t_wall1) if sampler is not None else {},
     }
     line.update(extras)
@@ -772,8 +771,9 @@ def seqshard_sub(args, rank: int, world: int, dev, timer):
            "value": wl.bytes_per_call / (ms * 1e-3) / 1e12, "unit": "TB/s (whole call, all ranks)",
            "bytes_per_call": wl.bytes_per_call, "steps": steps,
            "parallelism": (f"sequence-shard x{world}: one kernel per step, decode with the exchange fused into its "
-                           "epilogue (fs_paged_decode_exchange)" if world > 1 else "one GPU (decode + merge)"),
-           "gpu_launches_per_step": 1 if world > 1 else 2}
+                           "epilogue (fs_paged_decode_exchange)" if world > 1
+                           else "one GPU (plain decode of the whole sequence)"),
+           "gpu_launches_per_step": 1}
     if world > 1:  # the same step as decode + separate exchange kernel, for comparison
         ms_k, _ = timed("p2p_kernel")
         res["two_kernel_step"] = {"us_per_call": ms_k * 1e3, "value": wl.bytes_per_call / (ms_k * 1e-3) / 1e12,

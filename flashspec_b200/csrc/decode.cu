@@ -449,77 +449,102 @@ __device__ __forceinline__ void write_final(const DecodeParams& p, size_t row, i
   }
 }
 
+// Profiling aid of the split kernel (FLASHSPEC_TRACE_PTR): thread 0 stamps %globaltimer
+// into trace[k]; per CTA c: [4c] entry, [4c + 1] pages consumed, [4c + 2] partial
+// written; per pair q, from 4 * gridDim.x: [16q] merge start, [16q + 1] rows ready,
+// [16q + 2] exchange stores issued, [16q + 3] every rank's rows merged, [16q + 4] end,
+// [16q + 5] partial LSEs loaded, [16q + 6] weights formed, [16q + 7] partial rows
+// summed, [16q + 8 + 2r] staging round r arrived, [16q + 9 + 2r] round r summed.
+__device__ __forceinline__ void split_mark(const DecodeParams& p, size_t k) {
+  if (p.trace != nullptr && threadIdx.x == 0) p.trace[k] = globaltimer_ns();
+}
+
 // Fused exchange epilogue of a sequence-sharded step: this rank's normalised (O, LSE)
 // rows of pair (b, h) -- staged in shared memory as xo [G][128], xl [G] -- go as tagged
 // words (xwords.cuh) into slot `xrank` of every rank's exchange buffer; then the CTA
 // merges every rank's rows of the pair with the log-sum-exp rule (the combine of
 // triton_fused.py:446-503 on one partial per rank) as they arrive, and writes them to
 // xout.  Waits end at xtimeout_ns: the CTA then sets FS_DEV_TIMEOUT and writes NaN.
-// The pair's call counter in this rank's buffer gives the epoch (tag and parity).
+// The pair's call counter in this rank's buffer gives the epoch (tag and parity).  The
+// LSE words come first (one per rank and row, giving the weights), then the O words,
+// each thread loading all of its elements of a peer at once.
+template <int kThreads>
 __device__ __forceinline__ void exchange_pair(const DecodeParams& p, int b, int h, int bh, const float* xo,
-                                           const float* xl, int tid, int nthreads) {
+                                              float* xl, int tid) {
   uint8_t* own = static_cast<uint8_t*>(p.xbufs[p.xrank]);
   uint32_t* calls = reinterpret_cast<uint32_t*>(own + kXPairCountersOffset);
   const uint32_t e = calls[bh] + 1u;  // written by this pair's previous call on this GPU
   const size_t poff = exchange_parity_offset(e, p.xslot);
   const int64_t rows = (int64_t)p.B * p.Hq;
   const int64_t row0 = (int64_t)b * p.Hq + (int64_t)h * p.G;
-  const int n = p.G * kD;
+  const int G = p.G, n = G * kD;
   for (int r = 0; r < p.xworld; ++r) {
     if (r == p.xrank) continue;  // this rank's rows are merged from shared memory
     uint64_t* dst = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(p.xbufs[r]) + poff) + (size_t)p.xrank * p.xslot;
-    for (int i = tid; i < n; i += nthreads) st_word(dst + row0 * kD + i, xo[i], e);
-    if (tid < p.G) st_word(dst + rows * kD + row0 + tid, xl[tid], e);
+    for (int i = tid; i < n; i += kThreads) st_word(dst + row0 * kD + i, xo[i], e);
+    if (tid < G) st_word(dst + rows * kD + row0 + tid, xl[tid], e);
   }
+  const size_t tr = 4 * (size_t)gridDim.x + 16 * (size_t)bh;
+  split_mark(p, tr + 2);
   const uint64_t* data = reinterpret_cast<const uint64_t*>(own + poff);
   const uint64_t deadline = globaltimer_ns() + (uint64_t)p.xtimeout_ns;
+  // 1. every rank's LSE of the pair's G rows -> normalised weights w[r][q] in shared
+  //    memory (after xl); the output is O only, so the merged LSE is not formed
+  float* w = xl + kMaxG;  // [kXMaxRanks][kMaxG]
   bool ok = true;
-  for (int i = tid; i < n; i += nthreads) {
-    const int qg = i >> 7;
-    float lse[kXMaxRanks], o[kXMaxRanks];
-    uint64_t wl[kXMaxRanks], wo[kXMaxRanks];
-    // first look: every rank's two words at once (independent loads in flight)
-#pragma unroll
-    for (int r = 0; r < kXMaxRanks; ++r)
-      if (r < p.xworld && r != p.xrank) {
-        wl[r] = ld_word(data + (size_t)r * p.xslot + rows * kD + row0 + qg);
-        wo[r] = ld_word(data + (size_t)r * p.xslot + row0 * kD + i);
-      }
+  if (tid < p.xworld * G) {
+    const int r = tid / G, qg = tid - r * G;
+    float l = xl[qg];
+    if (r != p.xrank) ok = wait_word(data + (size_t)r * p.xslot + rows * kD + row0 + qg, e, deadline, l);
+    w[r * kMaxG + qg] = l;
+  }
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (tid < G) {
     float M = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < kXMaxRanks; ++r) {
-      lse[r] = -INFINITY;
-      o[r] = 0.f;
-      if (r >= p.xworld) continue;
-      if (r == p.xrank) {
-        lse[r] = xl[qg];
-        o[r] = xo[i];
-      } else if (ok) {
-        const uint64_t* pl = data + (size_t)r * p.xslot + rows * kD + row0 + qg;
-        const uint64_t* po = data + (size_t)r * p.xslot + row0 * kD + i;
-        if ((uint32_t)(wl[r] >> 32) == e)
-          lse[r] = __uint_as_float((uint32_t)wl[r]);
-        else
-          ok = wait_word(pl, e, deadline, lse[r]);
-        if (ok) {
-          if ((uint32_t)(wo[r] >> 32) == e)
-            o[r] = __uint_as_float((uint32_t)wo[r]);
-          else
-            ok = wait_word(po, e, deadline, o[r]);
-        }
-      }
-      M = fmaxf(M, lse[r]);
+    for (int r = 0; r < p.xworld; ++r) M = fmaxf(M, w[r * kMaxG + tid]);
+    float W = 0.f;
+    for (int r = 0; r < p.xworld; ++r) {
+      const float l = w[r * kMaxG + tid];
+      const float x = (M == -INFINITY || l == -INFINITY) ? 0.f : expf(l - M);
+      w[r * kMaxG + tid] = x;
+      W += x;
     }
-    float W = 0.f, O = 0.f;
-    if (ok && M != -INFINITY)
+    const float inv = W > 0.f ? 1.f / W : 0.f;
+    for (int r = 0; r < p.xworld; ++r) w[r * kMaxG + tid] *= inv;
+  }
+  __syncthreads();
+  // 2. the rows: per peer rank, every element of this thread is loaded at once (one
+  //    round trip), then any word still missing is waited for
+  constexpr int kPer = (kMaxG * kD + kThreads - 1) / kThreads;
+  float acc[kPer];
 #pragma unroll
-      for (int r = 0; r < kXMaxRanks; ++r)
-        if (r < p.xworld) {
-          const float w = lse[r] == -INFINITY ? 0.f : expf(lse[r] - M);
-          W += w;
-          O += w * o[r];
-        }
-    const float v = !ok ? __int_as_float(0x7fc00000) : W > 0.f ? O / W : 0.f;
+  for (int j = 0; j < kPer; ++j) {
+    const int i = tid + j * kThreads;
+    acc[j] = i < n ? w[p.xrank * kMaxG + (i >> 7)] * xo[i] : 0.f;
+  }
+  for (int r = 0; r < p.xworld && ok; ++r) {
+    if (r == p.xrank) continue;
+    const uint64_t* src = data + (size_t)r * p.xslot + row0 * kD;
+    uint64_t v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = tid + j * kThreads;
+      v[j] = i < n ? ld_word(src + i) : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = tid + j * kThreads;
+      if (i >= n || !ok) continue;
+      float o = __uint_as_float((uint32_t)v[j]);
+      if ((uint32_t)(v[j] >> 32) != e) ok = wait_word(src + i, e, deadline, o);
+      acc[j] = fmaf(w[r * kMaxG + (i >> 7)], o, acc[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = tid + j * kThreads;
+    if (i >= n) continue;
+    const float v = ok ? acc[j] : __int_as_float(0x7fc00000);
     const size_t at = (size_t)row0 * kD + i;
     if (p.xout_dtype == FS_F16)
       static_cast<__half*>(p.xout)[at] = __float2half_rn(v);
@@ -528,6 +553,7 @@ __device__ __forceinline__ void exchange_pair(const DecodeParams& p, int b, int 
   }
   if (!ok && p.xstatus != nullptr) atomicOr(p.xstatus, FS_DEV_TIMEOUT);
   __syncthreads();  // every thread has read this call's words before the epoch advances
+  split_mark(p, tr + 3);
   if (tid == 0) calls[bh] = e;
 }
 
@@ -572,15 +598,18 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   const int lo = (int)max(p.page_begin, (int64_t)0);
   const int hi = p.page_end > 0 ? (int)min(p.page_end, (int64_t)npages) : npages;
   const int span = hi > lo ? hi - lo : 0;
+  __shared__ alignas(8) uint64_t s_merge_bar;  // the final merge's bulk copies
   const int chunk = (span + S - 1) / S;
   const int p0 = min(lo + split * chunk, max(hi, lo));
   const int n = max(min(hi, p0 + chunk) - p0, 0);  // pages of this CTA
+  split_mark(p, 4 * (size_t)blockIdx.x);
 
   if (tid == 0) {
     for (int st = 0; st < kNS; ++st) {
       mbar_init(full_s + 8 * st, 2);
       mbar_init(empty_s + 8 * st, 1);
     }
+    mbar_init(smem_u32(&s_merge_bar), 1);
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -659,6 +688,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   __syncthreads();  // every page has been consumed, so no copy still targets the ring
   const bool any_abort = __syncthreads_or(aborted ? 1 : 0);
   if (any_abort) return;  // status word carries FS_DEV_TIMEOUT; outputs are not written
+  split_mark(p, 4 * (size_t)blockIdx.x + 1);
   float* ms = reinterpret_cast<float*>(base_p);
   float* ls = ms + kW * kMaxG;
   float* accs = ls + kW * kMaxG;  // [kW][kMaxG][kD]
@@ -684,43 +714,68 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   const int nout = p.G * kD;
   const float kLn2 = 0.6931471805599453f;
   // fused exchange: the pair's merged rows are staged at the end of the ring region
-  constexpr int kXStage = (L::kStageRegion - (kMaxG * kD + kMaxG) * 4) & ~15;
-  static_assert(kXStage >= (2 + kD) * kW * kMaxG * 4, "exchange staging overlaps the warp merge");
+  constexpr int kXStage = (L::kStageRegion - (kMaxG * kD + kMaxG + kXMaxRanks * kMaxG) * 4) & ~15;
+  static_assert(kXStage >= ((3 + kD) * kW * kMaxG + kMaxG) * 4, "exchange staging overlaps the warp merge");
   const bool xmode = p.xworld > 0;
   float* xo = reinterpret_cast<float*>(base_p + kXStage);
   float* xl = xo + kMaxG * kD;
-  for (int idx = tid; idx < nout; idx += kThreads) {
-    const int qg = idx >> 7;
-    const int d = idx & (kD - 1);
+  // per query: the warps' scale factors exp2(m_w - M) / L folded into one weight each,
+  // and the LSE, formed once (G threads) so the row loop below is loads and FMAs only
+  float* fw = accs + kW * kMaxG * kD;  // [kW][kMaxG] weights, then [kMaxG] LSE
+  float* flse = fw + kW * kMaxG;
+  if (tid < p.G) {
     float M = -1.0e30f;
 #pragma unroll
-    for (int w = 0; w < kW; ++w) M = fmaxf(M, ms[w * kMaxG + qg]);
-    float Lsum = 0.f, O = 0.f;
+    for (int w = 0; w < kW; ++w) M = fmaxf(M, ms[w * kMaxG + tid]);
+    float sc[kW], Lsum = 0.f;
 #pragma unroll
     for (int w = 0; w < kW; ++w) {
-      const float sc = exp2f(ms[w * kMaxG + qg] - M);
-      Lsum += ls[w * kMaxG + qg] * sc;
-      O += accs[(w * kMaxG + qg) * kD + d] * sc;
+      sc[w] = exp2f(ms[w * kMaxG + tid] - M);
+      Lsum += ls[w * kMaxG + tid] * sc[w];
     }
-    const float o = Lsum > 0.f ? O / Lsum : 0.f;
-    const float lse = Lsum > 0.f ? (M + log2f(Lsum)) * kLn2 : -INFINITY;
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+    for (int w = 0; w < kW; ++w) fw[w * kMaxG + tid] = sc[w] * inv;
+    flse[tid] = Lsum > 0.f ? (M + log2f(Lsum)) * kLn2 : -INFINITY;
+  }
+  __syncthreads();
+  for (int u4 = tid; u4 < nout / 4; u4 += kThreads) {
+    const int idx = 4 * u4;
+    const int qg = idx >> 7;
+    const int d = idx & (kD - 1);
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kW; ++w) {
+      const float f = fw[w * kMaxG + qg];
+      const float4 a4 = *reinterpret_cast<const float4*>(accs + (w * kMaxG + qg) * kD + d);
+      o.x = fmaf(a4.x, f, o.x);
+      o.y = fmaf(a4.y, f, o.y);
+      o.z = fmaf(a4.z, f, o.z);
+      o.w = fmaf(a4.w, f, o.w);
+    }
+    const float lse = flse[qg];
     const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
     if (S == 1 && xmode) {
-      xo[idx] = o;
+      *reinterpret_cast<float4*>(xo + idx) = o;
       if (d == 0) xl[qg] = lse;
     } else if (S == 1) {
-      write_final(p, row, d, o, lse);
+      write_final(p, row, d, o.x, lse);
+      write_final(p, row, d + 1, o.y, lse);
+      write_final(p, row, d + 2, o.z, lse);
+      write_final(p, row, d + 3, o.w, lse);
     } else {
       const size_t prow = ((size_t)bh * S + split) * p.G + qg;
-      p.part_o[prow * kD + d] = o;
+      *reinterpret_cast<float4*>(p.part_o + prow * kD + d) = o;
       if (d == 0) p.part_lse[prow] = lse;
     }
   }
   if (S == 1) {
     if (xmode) {
       __syncthreads();
-      exchange_pair(p, b, h, bh, xo, xl, tid, kThreads);
+      split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 1);
+      exchange_pair<kThreads>(p, b, h, bh, xo, xl, tid);
     }
+    split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 4);
     return;
   }
 
@@ -733,60 +788,109 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
     s_last = (ticket == (unsigned)(S - 1)) ? 1 : 0;
   }
   __syncthreads();
+  split_mark(p, 4 * (size_t)blockIdx.x + 2);
   if (!s_last) return;
   __threadfence();
-  // weights of the S partials per query, computed once into shared memory (the ring is
-  // free now): w[s][q] = exp(lse_s - M) / sum_s exp(lse_s - M); empty partials weigh 0
-  float* wsm = reinterpret_cast<float*>(base_p);  // [S][G] (+ [G] merged LSE)
+  split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh);
+  // the S partial LSEs of each query, staged in shared memory (the ring is free now)
+  float* wsm = reinterpret_cast<float*>(base_p);  // [S][G]
   const int nw = S * p.G;
-  const bool fits = (nw + p.G) * 4 <= kXStage;
+  const bool fits = (nw + 3 * kMaxG) * 4 + 1024 + p.G * kD * 4 <= kXStage;
+  // staging of the partial rows (bulk copies, below): the first round is issued before
+  // the weights are computed, so its latency overlaps theirs
+  const int rows_bytes = p.G * kD * 4;
+  const int stage_off = (((nw + 3 * kMaxG) * 4) + 1023) & ~1023;
+  const int per_round = max(1, (kXStage - stage_off) / rows_bytes);
+  const uint32_t mbar = smem_u32(&s_merge_bar);
+  const float* src0 = p.part_o + (size_t)bh * S * p.G * kD;
+  auto issue_round = [&](int s0) {
+    const int cnt = min(per_round, S - s0);
+    // the partials were written by other CTAs through the generic proxy, and the
+    // stage was last read through it
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(mbar, (uint32_t)(cnt * rows_bytes));
+    for (int u = 0; u < cnt; ++u)
+      bulk_load(base_s + stage_off + u * rows_bytes, src0 + (size_t)(s0 + u) * p.G * kD, (uint32_t)rows_bytes, mbar);
+  };
+  if (fits && tid == 0) issue_round(0);
   if (fits) {
     const size_t prow0 = (size_t)bh * S * p.G;
     for (int k = tid; k < nw; k += kThreads) wsm[k] = __ldcg(p.part_lse + prow0 + k);
     __syncthreads();
-    if (tid < p.G) {
-      float M = -INFINITY;
-      for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, wsm[s2 * p.G + tid]);
-      float W = 0.f;
-      if (M != -INFINITY)
-        for (int s2 = 0; s2 < S; ++s2) {
-          const float l = wsm[s2 * p.G + tid];
-          const float w = l == -INFINITY ? 0.f : expf(l - M);
-          wsm[s2 * p.G + tid] = w;
-          W += w;
-        }
-      const float inv = W > 0.f ? 1.f / W : 0.f;
-      for (int s2 = 0; s2 < S; ++s2) wsm[s2 * p.G + tid] = M == -INFINITY ? 0.f : wsm[s2 * p.G + tid] * inv;
-      wsm[nw + tid] = W > 0.f ? M + logf(W) : -INFINITY;
-    }
-    __syncthreads();
+    split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 5);
   }
   if (fits) {
-    // every split wrote its partial row (an empty one with weight 0), so each thread
-    // streams 4 head dims of a query over all splits, eight 16-byte loads in flight
-    constexpr int kBatch = 8;
-    const size_t stride = (size_t)p.G * kD;  // floats between splits
-    for (int u4 = tid; u4 < nout / 4; u4 += kThreads) {
-      const int qg = (4 * u4) >> 7;
-      const int d = (4 * u4) & (kD - 1);
-      const float* src = p.part_o + ((size_t)bh * S * p.G + qg) * kD + d;
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s0 = 0; s0 < S; s0 += kBatch) {
-        float4 v[kBatch];
+    // every split wrote its partial rows [G][128] (an empty one with weight 0), 4 KB
+    // contiguous per split at most: bulk copies stage them in shared memory behind the
+    // LSEs, as many splits per round as fit, so a round costs one copy latency
+    const float* stage_p = reinterpret_cast<const float*>(base_p + stage_off);
+    // weights w[s][q] = exp(lse_s - M_q) (empty partials 0) in place of the LSEs, each
+    // phase spread over the threads so that no thread runs a long dependent chain;
+    // 1 / sum_s w and the merged LSE per query go behind them
+    float* wM = wsm + nw;  // [G] max, then [G] 1 / W, then [G] merged LSE
+    float* wI = wM + kMaxG;
+    float* wL = wI + kMaxG;
+    if (tid < p.G) {
+      float M = -INFINITY;
+#pragma unroll 8
+      for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, wsm[s2 * p.G + tid]);
+      wM[tid] = M;
+    }
+    __syncthreads();
+    for (int k = tid; k < nw; k += kThreads) {
+      const float l = wsm[k], M = wM[k % p.G];
+      wsm[k] = (l == -INFINITY || M == -INFINITY) ? 0.f : expf(l - M);
+    }
+    __syncthreads();
+    if (tid < p.G) {
+      float W = 0.f;
+#pragma unroll 8
+      for (int s2 = 0; s2 < S; ++s2) W += wsm[s2 * p.G + tid];
+      wI[tid] = W > 0.f ? 1.f / W : 0.f;
+      wL[tid] = W > 0.f ? wM[tid] + logf(W) : -INFINITY;
+    }
+    split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 6);
+    // each thread accumulates 4 head dims of a query per column
+    constexpr int kCols = (kMaxG * kD / 4 + kThreads - 1) / kThreads;
+    float4 acc[kCols];
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u)
-          v[u] = s0 + u < S ? __ldcg(reinterpret_cast<const float4*>(src + (size_t)(s0 + u) * stride))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c4 = 0; c4 < kCols; ++c4) acc[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+    int round = 0;
+    for (int s0 = 0; s0 < S; s0 += per_round, ++round) {
+      const int cnt = min(per_round, S - s0);
+      if (tid == 0 && s0 > 0) issue_round(s0);
+      if (!mbar_spin_bounded(mbar, (uint32_t)(round & 1), kTimeoutNs) && tid == 0 && p.status != nullptr)
+        atomicOr(p.status, FS_DEV_TIMEOUT);
+      if (round < 4) split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 8 + 2 * round);
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-          const float w = s0 + u < S ? wsm[(s0 + u) * p.G + qg] : 0.f;
-          o.x = fmaf(w, v[u].x, o.x);
-          o.y = fmaf(w, v[u].y, o.y);
-          o.z = fmaf(w, v[u].z, o.z);
-          o.w = fmaf(w, v[u].w, o.w);
+      for (int c4 = 0; c4 < kCols; ++c4) {
+        const int u4 = tid + c4 * kThreads;
+        if (u4 >= nout / 4) continue;
+        const int qg = (4 * u4) >> 7;
+#pragma unroll 7
+        for (int u = 0; u < cnt; ++u) {
+          const float w = wsm[(s0 + u) * p.G + qg];
+          const float4 v = *reinterpret_cast<const float4*>(stage_p + (size_t)u * p.G * kD + 4 * u4);
+          acc[c4].x = fmaf(w, v.x, acc[c4].x);
+          acc[c4].y = fmaf(w, v.y, acc[c4].y);
+          acc[c4].z = fmaf(w, v.z, acc[c4].z);
+          acc[c4].w = fmaf(w, v.w, acc[c4].w);
         }
       }
-      const float lse_out = wsm[nw + qg];
+      __syncthreads();  // the stage is free for the next round
+      if (round < 4) split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 9 + 2 * round);
+    }
+    split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 7);
+#pragma unroll
+    for (int c4 = 0; c4 < kCols; ++c4) {
+      const int u4 = tid + c4 * kThreads;
+      if (u4 >= nout / 4) continue;
+      const int qg = (4 * u4) >> 7;
+      const int d = (4 * u4) & (kD - 1);
+      const float inv = wI[qg];
+      const float4 o = make_float4(acc[c4].x * inv, acc[c4].y * inv, acc[c4].z * inv, acc[c4].w * inv);
+      const float lse_out = wL[qg];
       const size_t row = (size_t)b * p.Hq + (size_t)h * p.G + qg;
       if (xmode) {
         *reinterpret_cast<float4*>(xo + 4 * u4) = o;
@@ -830,8 +934,10 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
   if (tid == 0) p.counters[bh] = 0u;  // leave the ticket clean for the next call
   if (xmode) {
     __syncthreads();
-    exchange_pair(p, b, h, bh, xo, xl, tid, kThreads);
+    split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 1);
+    exchange_pair<kThreads>(p, b, h, bh, xo, xl, tid);
   }
+  split_mark(p, 4 * (size_t)gridDim.x + 16 * (size_t)bh + 4);
 }
 
 // ==================================================================================
@@ -1319,7 +1425,8 @@ __host__ DecodeKernelFn balanced_inst() {
 
 // FLASHSPEC_TRACE_PTR (profiling only): device address of a zeroed uint64 buffer of
 // ctas * (warps + 1) * 8 words; the balanced kernel of shape 0 then records its
-// per-warp timeline there (trace_mark).
+// per-warp timeline there (trace_mark), the split kernel its per-CTA and per-pair
+// timeline (4 * ctas + 8 * pairs words, split_mark).
 static unsigned long long* trace_ptr() {
   const char* v = getenv("FLASHSPEC_TRACE_PTR");
   return v ? reinterpret_cast<unsigned long long*>(strtoull(v, nullptr, 0)) : nullptr;

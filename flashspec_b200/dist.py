@@ -266,6 +266,9 @@ class SequenceShardedDecoder:
             if self.check_every > 0 and self._calls % self.check_every == 0:
                 xch.check()
             return out
+        if self.world == 1 and out_dtype == q.dtype:
+            # one rank holds the whole window: the plain decode writes the output itself
+            return paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages))
         paged_quant_attention_cuda(q, cache, page_range=self.window(n_pages), partial_out=(o, lse))
         if self.world > 1:  # out of place: the send buffer is not a view of the receive buffer
             dist.all_gather_into_tensor(gather.view(-1), mine, group=self.group)
