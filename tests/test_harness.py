@@ -86,3 +86,28 @@ def test_profile_matrix_dry_run(tmp_path):
         got = list(csv.DictReader(f))
     assert [r["seq_len"] for r in got] == ["2048", "2048", "4096", "4096"]
     assert all(r["error"].startswith("dry-run") for r in got)
+
+
+def test_split_timeline_phases_reads_the_trace_layout():
+    """The timeline reader maps the kernel's stamp layout (4 words per CTA, 16 per pair)."""
+    import numpy as np
+
+    from flashspec_b200.harness.split_timeline import _phases
+
+    ctas, pairs, t0 = 6, 2, 1_000_000
+    buf = np.zeros(4 * ctas + 16 * pairs, dtype=np.int64)
+    for c in range(ctas):
+        buf[4 * c: 4 * c + 3] = [t0 + 100 * c, t0 + 10_000 + 100 * c, t0 + 12_000]
+    for q in range(pairs):
+        base = 4 * ctas + 16 * q
+        start = t0 + 13_000 + 500 * q
+        buf[base] = start
+        buf[base + 4] = start + 5_000
+        buf[base + 5] = start + 1_000
+    out = _phases(buf, ctas, pairs, t0)
+    assert out["cta_entry_first_last"] == [0.0, 0.5]
+    assert out["stream_done_first_median_last"][0] == 10.0
+    assert out["end_last"] == 18.5
+    assert out["last_pair_merge_from_its_start"]["lse_loaded"] == 1.0
+    assert out["last_pair_merge_from_its_start"]["end"] == 5.0
+    assert out["last_pair_merge_from_its_start"]["round1_arrived"] is None
