@@ -51,7 +51,14 @@ constexpr int kStageBytes = 2 * kPageBytes;  // K + V
 constexpr int kMetaBytes = 160;  // 32 bytes of page qparams + 128 bytes of per-token scales
 constexpr int kMaxG = 8;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-constexpr uint32_t kProducerSleepNs = 1000;  // suspend hint of the producer's free-stage waits
+constexpr uint32_t kProducerSleepNs = 1000;  // default suspend hint of the producer's free-stage waits
+
+// The producer's wait for a free stage: suspending (with a time hint) leaves issue slots
+// to the consumer warps; hint 0 spins.
+__device__ __forceinline__ bool producer_wait(uint32_t bar, uint32_t parity, int sleep_ns) {
+  return sleep_ns > 0 ? mbar_wait_sleepy(bar, parity, (uint32_t)sleep_ns, kTimeoutNs)
+                      : mbar_spin_bounded(bar, parity, kTimeoutNs);
+}
 
 struct DecodeParams {
   const __half* q;
@@ -79,6 +86,7 @@ struct DecodeParams {
   int piece_cost;       // balanced kernel: virtual pages charged per (request, kv head) pair
   int debug_mode;       // profiling only (FLASHSPEC_DEBUG_MODE)
   int sym;              // FS_KV_SYMMETRIC: per-token scales [blocks, 16], no zero points
+  int producer_sleep_ns;  // suspend hint of the producer's free-stage waits; 0 = spin
   // fused exchange epilogue (fs_paged_decode_exchange); xworld == 0 otherwise
   void* xbufs[kXMaxRanks];
   void* xout;
@@ -645,7 +653,7 @@ __global__ void __launch_bounds__((kW + 1) * 32, kMinBlocks)
       const int i = i0 + lane;
       if (lane < kIssue && i < n) {
         const int st = (int)((unsigned)i % kNS);
-        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (((unsigned)i / kNS) - 1u) & 1u, kProducerSleepNs, kTimeoutNs)) {
+        if (i >= kNS && !producer_wait(empty_s + 8 * st, (((unsigned)i / kNS) - 1u) & 1u, p.producer_sleep_ns)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
@@ -1241,7 +1249,7 @@ __global__ void __maxnreg__(kMaxRegs)
       const int i = i0 + lane;
       if (lane < kIssue && e != -2) {
         const int st = (int)((unsigned)i % kNS);
-        if (i >= kNS && !mbar_wait_sleepy(empty_s + 8 * st, (((unsigned)i / kNS) - 1u) & 1u, kProducerSleepNs, kTimeoutNs)) {
+        if (i >= kNS && !producer_wait(empty_s + 8 * st, (((unsigned)i / kNS) - 1u) & 1u, p.producer_sleep_ns)) {
           if (p.status != nullptr) atomicOr(p.status, FS_DEV_TIMEOUT);
           aborted = true;
         }
@@ -1682,6 +1690,15 @@ static int piece_cost() {
   return kDefaultPieceCost;
 }
 
+// FLASHSPEC_PRODUCER_SLEEP_NS overrides the producer's suspend hint (profiling; 0 spins).
+static int producer_sleep_ns() {
+  if (const char* v = getenv("FLASHSPEC_PRODUCER_SLEEP_NS")) {
+    const int n = atoi(v);
+    if (n >= 0 && n <= 100000) return n;
+  }
+  return (int)kProducerSleepNs;
+}
+
 // FLASHSPEC_DECODE_KERNEL=split|balanced forces a kernel (profiling, tests).
 static int kernel_override() {
   const char* v = getenv("FLASHSPEC_DECODE_KERNEL");
@@ -1884,6 +1901,7 @@ static int launch_decode(const FsDecodeArgs* a_in, void* stream, const FsExchang
   p.piece_cost = piece_cost();
   p.debug_mode = debug_mode();
   p.sym = a->kv_format == FS_KV_SYMMETRIC;
+  p.producer_sleep_ns = producer_sleep_ns();
   if (x != nullptr) {
     for (int r = 0; r < x->world; ++r) p.xbufs[r] = x->bufs[r];
     p.xout = x->out;
