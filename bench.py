@@ -484,10 +484,18 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
         decoder = SequenceShardedDecoder()
         n_pages = wl.cache.block_table.shape[1]
-        replay, _ = decoder.capture(wl.q, wl.cache, n_pages)
+        # graphs of kSeqGraph steps (and a one-step graph for a remainder): every step is
+        # one decode call, without the start of a graph launch between most of them
+        replay_n, _ = decoder.capture(wl.q, wl.cache, n_pages, steps=kSeqGraph)
+        replay_1, _ = decoder.capture(wl.q, wl.cache, n_pages)
 
-        def step(i):
-            replay()
+        def step(i, total=None):
+            total = total or args.steps
+            full = total // kSeqGraph * kSeqGraph
+            if i >= full:
+                replay_1()
+            elif i % kSeqGraph == 0:
+                replay_n()
     else:
         def step(i):
             return fs.paged_quant_attention_cuda(wl.q, wl.cache, num_splits=wl.num_splits)
@@ -508,7 +516,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # ---- device-resident timed region ----------------------------------------------------
     elapsed_ms = timer.run(step, args.steps)
     t_wall1 = time.time()
-    host_us = host_us_per_call(lambda: step(0))
+    host_us = (host_us_per_call(replay_n) / kSeqGraph if seqshard and args.steps >= kSeqGraph
+               else host_us_per_call(lambda: step(0)))
 
     # ---- end-to-end through the public API with host buffers -----------------------------
     q = wl.q
@@ -612,7 +621,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                                    else f"request-shard x{world}" if world > 1 else "single"),
                    "l2": ("four rotated input copies (135 MB each, > L2 together)" if fused
                           else "inputs larger than L2 (no flush)"),
-                   "bytes_per_call_per_gpu": launch_bytes},
+                   "bytes_per_call_per_gpu": launch_bytes,
+                   **({"cuda_graph": f"{kSeqGraph} steps per graph replay"} if seqshard else {})},
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": "TB/s", "h2d_bytes_per_step": pipe.h2d_bytes,
                 "d2h_bytes_per_step": pipe.d2h_bytes, "us_per_call": e2e_ms / e2e_steps * 1e3,
@@ -742,6 +752,9 @@ def other_configs(args, timer, dev):
     return res
 
 
+kSeqGraph = 10  # sequence-sharded steps recorded per CUDA graph
+
+
 def seqshard_sub(args, rank: int, world: int, dev, timer):
     """cfg3 (B2, 64q/8kv, 131072 tokens) split by page windows over the N ranks and merged
     through the peer-memory exchange; rank 0 checks its merged output against a
@@ -754,14 +767,14 @@ def seqshard_sub(args, rank: int, world: int, dev, timer):
 
     wl = configs.cfg3_shard(rank, world)
     n_pages = int(wl.cache.block_table.shape[1])
-    steps = max(20, min(args.steps, 2000))
+    steps = max(20, min(args.steps, 2000)) // kSeqGraph * kSeqGraph
 
     def timed(transport):
         dec = SequenceShardedDecoder(transport=transport)
-        replay, out = dec.capture(wl.q, wl.cache, n_pages)
+        replay, out = dec.capture(wl.q, wl.cache, n_pages, steps=kSeqGraph)
         for _ in range(max(3, args.warmup)):
             replay()
-        ms = timer.run(lambda i: replay(), steps) / steps
+        ms = timer.run(lambda i: replay() if i % kSeqGraph == 0 else None, steps) / steps
         torch.cuda.synchronize()
         dec.close()  # raises if an exchange timed out
         return ms, out

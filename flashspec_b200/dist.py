@@ -322,12 +322,16 @@ class SequenceShardedDecoder:
         if failure is not None:
             raise failure
 
-    def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16):
-        """Record the decode step of a single-rank group (partial kernel + merge) as a CUDA
-        graph over the given tensors; returns ``(replay, out)`` where ``replay()`` re-runs
-        the step on the current contents of q / cache and refreshes ``out``.  Multi-rank
-        steps are captured only with the peer-memory exchange (the NCCL step runs eagerly);
-        every rank must then replay its graph the same number of times."""
+    def capture(self, q: torch.Tensor, cache, n_pages: int, out_dtype: torch.dtype = torch.float16,
+                steps: int = 1):
+        """Record ``steps`` consecutive decode steps as one CUDA graph over the given
+        tensors; returns ``(replay, out)`` where ``replay()`` re-runs them on the current
+        contents of q / cache and refreshes ``out`` (the last step's output).  Several
+        steps per graph spare the device the start of a graph launch between steps.
+        Multi-rank steps are captured only with the peer-memory exchange (the NCCL step
+        runs eagerly); every rank must then replay its graphs the same number of steps."""
+        if steps < 1:
+            raise ValueError("steps must be >= 1")
         if self.world > 1 and self.transport == "nccl":
             raise ValueError("capture() of a multi-rank step needs a p2p transport; NCCL steps run eagerly")
         side = torch.cuda.Stream(device=q.device)
@@ -338,5 +342,6 @@ class SequenceShardedDecoder:
         torch.cuda.current_stream(q.device).wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            out = self(q, cache, n_pages, out_dtype)
+            for _ in range(steps):
+                out = self(q, cache, n_pages, out_dtype)
         return graph.replay, out
